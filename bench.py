@@ -1,0 +1,401 @@
+"""Benchmark of the vllm-jax B200 hot path (one JSON line on rank 0).
+
+Default workload: paged decode attention at the Qwen3-8B
+head shape -- batch 256, one query token per sequence, context lengths
+log-uniform in [512, 32768] (seed 0), block_size 16, block tables drawn from a
+random permutation of a 200k-block pool, bf16 K/V ~ N(0, 1). Metric: paged-
+decode HBM GB/s (algorithmic bytes / time). One "step" = one decode-attention
+call over the whole batch (all KV heads of all sequences).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload decode|prefill]
+
+N > 1 (torchrun, one process per GPU): tensor parallel by KV head -- rank r
+owns KV heads [r*8/N, (r+1)*8/N) of the same batch (its own pool slice); no
+collective on the data path. Total work is fixed, so scaling is "strong";
+`value` = algorithmic bytes of all ranks / max-over-ranks device time.
+
+--impl reference times the reference algorithm on the host CPU cores: the
+reference (JAX/Pallas) cannot be installed in this image, so its NumPy
+restatement in oracle/ runs instead (cpu_baseline.kind = "port").
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "vllm-jax_b200"))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+# C3
+C3 = dict(batch=256, num_q_heads=32, num_kv_heads=8, head_dim=128, block_size=16,
+          ctx_min=512, ctx_max=32768, pool_blocks=200_000, table_width=2048, seed=0)
+# C2
+C2 = dict(num_seqs=64, num_q_heads=32, num_kv_heads=8, head_dim=128, block_size=16,
+          new_min=128, new_max=4096, prefix_min=0, prefix_max=2048, pool_blocks=200_000,
+          seed=0)
+
+
+def c3_lengths(cfg=C3) -> np.ndarray:
+    rng = np.random.default_rng(cfg["seed"])
+    u = rng.uniform(math.log(cfg["ctx_min"]), math.log(cfg["ctx_max"]), cfg["batch"])
+    return np.round(np.exp(u)).astype(np.int32)
+
+
+def c3_block_tables(lens: np.ndarray, cfg=C3) -> np.ndarray:
+    rng = np.random.default_rng(cfg["seed"] + 1)
+    perm = rng.permutation(cfg["pool_blocks"]).astype(np.int32)
+    bt = np.full((len(lens), cfg["table_width"]), -1, np.int32)
+    used = 0
+    for b, L in enumerate(lens):
+        n = (int(L) + cfg["block_size"] - 1) // cfg["block_size"]
+        bt[b, :n] = perm[used:used + n]
+        used += n
+    return bt
+
+
+def decode_bytes(lens: np.ndarray, hkv: int, hq: int, d: int = 128, bs: int = 16) -> int:
+    """Algorithmic HBM bytes of one decode call: K+V rows of every context token,
+    q in + out, the used block-table entries and the lengths."""
+    lens = lens.astype(np.int64)
+    kv = int(lens.sum()) * hkv * d * 2 * 2
+    qo = len(lens) * hq * d * 2 * 2
+    bt = int(((lens + bs - 1) // bs).sum()) * 4 + len(lens) * 4
+    return kv + qo + bt
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.out = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self) -> dict:
+        if not self.out:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle port), bounded sample
+# ---------------------------------------------------------------------------
+def _cpu_decode_seq(args):
+    L, hkv, g, seed = args
+    from oracle import attention as oatt
+    rng = np.random.default_rng(seed)
+    bs, d = 16, 128
+    npg = (L + bs - 1) // bs
+    kc = rng.standard_normal((npg, bs, hkv, d), dtype=np.float32)
+    vc = rng.standard_normal((npg, bs, hkv, d), dtype=np.float32)
+    q = rng.standard_normal((1, hkv * g, d), dtype=np.float32)
+    bt = np.arange(npg, dtype=np.int32)[None]
+    t0 = time.perf_counter()
+    oatt.decode_attention(q, kc, vc, bt, np.array([L], np.int32), 1 / math.sqrt(d))
+    return time.perf_counter() - t0
+
+
+def cpu_decode_baseline(lens: np.ndarray, hkv: int, hq: int, budget_s: float, pool) -> dict:
+    """Time the oracle on a seeded subsample of sequences with all host cores."""
+    rng = np.random.default_rng(123)
+    order = rng.permutation(len(lens))
+    cores = pool._processes if pool is not None else 1
+    done, sample, t_cpu = 0, [], 0.0
+    batch = max(1, cores)
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s and done < len(order):
+        idx = order[done:done + batch]
+        done += len(idx)
+        args = [(int(lens[i]), hkv, hq // hkv, int(i)) for i in idx]
+        times = (pool.map(_cpu_decode_seq, args) if pool is not None
+                 else [_cpu_decode_seq(a) for a in args])
+        t_cpu += float(sum(times))
+        sample.extend(int(i) for i in idx)
+    t_eff = t_cpu / cores  # compute seconds spread over the worker processes
+    sb = decode_bytes(lens[sample], hkv, hq)
+    return {"value": sb / t_eff / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"{len(sample)} of {len(lens)} C3 sequences "
+                      f"({int(lens[sample].sum())} ctx tokens) through the numpy oracle "
+                      f"(oracle/attention.py:decode_attention), one sequence per process; "
+                      f"{t_cpu:.1f} s of compute over {cores} processes"}
+
+
+def make_pool():
+    import multiprocessing as mp
+    n = len(os.sched_getaffinity(0))
+    return mp.get_context("spawn").Pool(n)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from vllm_b200.kernels.decode_paged_attention import paged_decode
+
+    cfg = C3
+    pool = make_pool() if (rank == 0 and not args.no_cpu_baseline) else None
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    hkv_all, hq_all = cfg["num_kv_heads"], cfg["num_q_heads"]
+    if hkv_all % world:
+        raise SystemExit(f"--gpus {world} must divide {hkv_all} KV heads")
+    hkv = hkv_all // world
+    hq = hq_all // world
+    lens = c3_lengths()
+    bt = c3_block_tables(lens)
+    B, nb, bs, D = cfg["batch"], cfg["pool_blocks"], cfg["block_size"], cfg["head_dim"]
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 + rank)
+    kv_cache = torch.empty((2, nb, bs, hkv, D), dtype=torch.bfloat16, device=dev)
+    for i in range(2):
+        for c in range(0, nb, 20000):
+            kv_cache[i, c:c + 20000].normal_(generator=gen)
+    q = torch.randn((B, hq, D), generator=gen, device=dev).to(torch.bfloat16)
+    d_bt = torch.from_numpy(bt).to(dev)
+    d_len = torch.from_numpy(lens).to(dev)
+    out = torch.empty_like(q)
+    scale = 1.0 / math.sqrt(D)
+
+    def step():
+        paged_decode(q, kv_cache, d_bt, d_len, scale, out=out)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        t_start.record(stream)
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            step()
+            ev[i][1].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    total_ms = t_start.elapsed_time(t_end)
+    per_launch_ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
+
+    # e2e through the public API with host buffers: H2D of q, block tables and
+    # lengths from pinned memory, the call, D2H of the output, every step.
+    h_q = q.cpu().pin_memory()
+    h_bt = torch.from_numpy(bt).pin_memory()
+    h_len = torch.from_numpy(lens).pin_memory()
+    h_out = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    e_q, e_bt, e_len = torch.empty_like(q), torch.empty_like(d_bt), torch.empty_like(d_len)
+
+    def e2e_step():
+        e_q.copy_(h_q, non_blocking=True)
+        e_bt.copy_(h_bt, non_blocking=True)
+        e_len.copy_(h_len, non_blocking=True)
+        paged_decode(e_q, kv_cache, e_bt, e_len, scale, out=out)
+        h_out.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+
+    t = torch.tensor([total_ms, per_launch_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, per_launch_ms, e2e_ms = t.tolist()
+    if rank != 0:
+        return
+    step_bytes = decode_bytes(lens, hkv_all, hq_all)      # all ranks together
+    rank_bytes = decode_bytes(lens, hkv, hq)               # one launch on one GPU
+    value = step_bytes * args.steps / (total_ms / 1e3) / 1e9
+    e2e_val = step_bytes * args.steps / (e2e_ms / 1e3) / 1e9
+    peaks, peak_src = load_peaks()
+    achieved = rank_bytes / (per_launch_ms / 1e3) / 1e9
+    cpu = (cpu_decode_baseline(lens, hkv_all, hq_all, args.cpu_budget, pool)
+           if pool is not None and world == 1 else None)
+    h2d = h_q.numel() * 2 + h_bt.numel() * 4 + h_len.numel() * 4
+    line = {
+        "metric": "paged-decode HBM GB/s (C3: Qwen3-8B heads, B=256, ctx log-U[512,32768])",
+        "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(total_ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded C3 lengths/tables; K,V,q ~ N(0,1) bf16)",
+        "config": {"workload": "C3 paged decode attention", "batch": B,
+                   "num_q_heads": hq_all, "num_kv_heads": hkv_all, "head_dim": D,
+                   "block_size": bs, "pool_blocks": nb, "table_width": C3["table_width"],
+                   "ctx_tokens": int(lens.sum()),
+                   "parallelism": f"tp{world} by KV head" if world > 1 else "single GPU",
+                   "l2": f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB read per step)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "peak_source": f"{peak_src} hbm_gbs",
+                     "kernel": "vj_paged_decode (plan + chunk + combine launches)",
+                     "traffic": DECODE_TRAFFIC_PER_LAUNCH if world == 1 else None},
+        "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": h_out.numel() * 2},
+        "gpu_launches": 3 * args.steps,
+        "clocks": clk.summary(),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    if pool is not None:
+        pool.terminate()
+
+
+# DRAM bytes (read + write) of one full C3 vj_paged_decode call on one GPU,
+# from the ncu capture summarised in profiles/ (None until captured).
+DECODE_TRAFFIC_PER_LAUNCH = None
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference's algorithm on host CPU cores (oracle port)
+# ---------------------------------------------------------------------------
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    pool = make_pool()
+    lens = c3_lengths()
+    hkv, hq = C3["num_kv_heads"], C3["num_q_heads"]
+    # each step: a bounded sample of the C3 batch (budget split over the steps)
+    budget = max(1.0, args.ref_budget / max(args.steps + args.warmup, 1))
+    for _ in range(args.warmup):
+        cpu_decode_baseline(lens, hkv, hq, budget, pool)
+    vals, samples = [], []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        r = cpu_decode_baseline(lens, hkv, hq, budget, pool)
+        vals.append(r["value"])
+        samples.append(r)
+    wall = time.perf_counter() - t0
+    v = float(np.mean(vals))
+    line = {
+        "impl": "reference",
+        "metric": "paged-decode HBM GB/s (C3: Qwen3-8B heads, B=256, ctx log-U[512,32768])",
+        "value": round(v, 4), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(wall / args.steps * 1e3, 1),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded C3 lengths)",
+        "config": {"workload": "C3 paged decode attention", "batch": C3["batch"],
+                   "num_q_heads": hq, "num_kv_heads": hkv, "head_dim": 128, "block_size": 16},
+        "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": samples[-1]["cores"],
+                         "kind": "port", "sample": samples[-1]["sample"]},
+        "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "jax/flax are not installable in this image (no network); the reference's "
+                "paged-attention algorithm runs as its NumPy restatement (oracle/).",
+    }
+    print(json.dumps(line), flush=True)
+    pool.terminate()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["decode"], default="decode")
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--ref-budget", type=float, default=60.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

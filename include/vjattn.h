@@ -1,0 +1,129 @@
+/*
+ * vjattn.h -- C ABI of the B200 (sm_100a) paged-attention hot path of
+ * vllm-jax: KV-slot scatter fused with Qwen3 q/k RMSNorm + RoPE, split-KV
+ * paged decode attention, varlen paged prefill attention, and the GPU
+ * builder of the ragged batch metadata.
+ *
+ * Conventions shared by every entry point
+ *   - All tensor arguments are DEVICE pointers owned by the caller (JAX
+ *     buffers through an XLA FFI shim, torch tensors, or raw cudaMalloc).
+ *     Dense activations are row-major bf16, indices are int32.
+ *   - Nothing here allocates device memory. Kernels that need scratch take a
+ *     caller-sized workspace whose size comes from a *_workspace_size query.
+ *   - Every call is asynchronous on the given stream and never synchronises
+ *     the host. Calls are reentrant; there is no hidden per-call state.
+ *   - The return value is a vj_status. On a nonzero status nothing was
+ *     launched and vj_get_last_error() returns a message for this thread.
+ *   - KV pages are addressed by (block, token-in-block, kv-head, dim) with
+ *     element strides, so both the engine's cache layout
+ *     (2, num_blocks, block_size, Hkv, D) and the Pallas kernels' page
+ *     layout (Hkv, num_blocks, page_size, D) are accepted without a copy.
+ *
+ * Reference interfaces replaced (paths inside the vllm-jax project):
+ *   vj_kv_store_qknorm_rope   vllm/model/qwen3.py:105-111 (_update_kv_cache),
+ *                             :59-78 (apply_rope), :286-296 (q/k norm+rope)
+ *   vj_paged_decode           vllm/kernels/decode_paged_attention.py:300-397
+ *                             (decode_paged_attention) incl. combine :274-283
+ *   vj_paged_prefill          vllm/kernels/prefill_paged_attention.py:407-453
+ *                             (prefill_paged_attention)
+ *   vj_build_metadata         vllm/src/model_runner.py:204-301
+ *                             (pad_block_tables, prepare_prefill, prepare_decode)
+ */
+#ifndef VJATTN_H_
+#define VJATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#ifndef __CUDA_RUNTIME_H__
+typedef struct CUstream_st *cudaStream_t;
+#endif
+
+#if defined(__GNUC__)
+#define VJ_API __attribute__((visibility("default")))
+#else
+#define VJ_API
+#endif
+
+typedef int vj_status;
+enum {
+  VJ_OK = 0,
+  VJ_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad shape, bad stride */
+  VJ_ERR_UNSUPPORTED = 2,      /* valid but not implemented (e.g. head_dim != 128) */
+  VJ_ERR_WORKSPACE = 3,        /* workspace missing or too small */
+  VJ_ERR_CUDA = 4              /* a CUDA runtime/driver call failed */
+};
+
+/* Flags of vj_kv_store_qknorm_rope. */
+enum {
+  VJ_KV_NORM = 1,          /* apply per-head RMSNorm to q and k (weights required) */
+  VJ_KV_ROPE = 2,          /* apply interleaved-pair RoPE to q and k */
+  VJ_KV_WRAP_NEGATIVE = 4  /* slot s<0 writes slot s+num_slots, as JAX .at[] does */
+};
+
+/* Message of the last failed call on this host thread ("" if none). */
+VJ_API const char *vj_get_last_error(void);
+
+/* ABI version: (major << 16) | minor. */
+VJ_API int vj_version(void);
+
+/* ---------------------------------------------------------------------------
+ * K3: q/k RMSNorm + RoPE + KV-slot scatter, one launch per layer.
+ * Replaces vllm/model/qwen3.py:105-111 (_update_kv_cache, mode="drop") and
+ * the q_norm/k_norm/apply_rope chain at qwen3.py:286-296 (apply_rope :59-78).
+ *
+ *   q_in [T,Hq,D], k_in [T,Hkv,D], v_in [T,Hkv,D]  bf16, token rows contiguous
+ *   q_norm_w, k_norm_w [D] bf16 (required with VJ_KV_NORM)
+ *   positions [T] int32, slot_mapping [T] int32 (flat slot = block*bs + offset)
+ *   q_out [T,Hq,D] bf16 (may equal q_in), k_out [T,Hkv,D] bf16 or NULL
+ *   k_cache/v_cache: element (blk,t,h,d) at base + blk*sb + t*st + h*sh + d
+ * Slots outside [0, num_blocks*block_size) are dropped (after the optional
+ * negative wrap). Numerics: sum of squares accumulated in fp64, rounded to
+ * fp32; every later step is a correctly rounded fp32 op followed by bf16
+ * round-to-nearest-even, so the result is reproducible bit for bit.
+ * ------------------------------------------------------------------------- */
+VJ_API vj_status vj_kv_store_qknorm_rope(
+    const void *q_in, const void *k_in, const void *v_in,
+    const void *q_norm_w, const void *k_norm_w,
+    const int32_t *positions, const int32_t *slot_mapping,
+    void *q_out, void *k_out, void *k_cache, void *v_cache,
+    int64_t num_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+    int32_t head_dim, int64_t num_blocks, int32_t block_size,
+    int64_t stride_block, int64_t stride_token, int64_t stride_head,
+    float eps, float rope_theta, int32_t flags, cudaStream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * K2: split-KV paged decode attention (one query token per sequence).
+ * Replaces vllm/kernels/decode_paged_attention.py:300-397 together with its
+ * XLA combine (:274-283) and the q scaling at vllm/model/qwen3.py:207.
+ *
+ *   q [B,Hq,D] bf16, out [B,Hq,D] bf16
+ *   block_tables [B, bt_width] int32, row stride bt_stride (entries <0 are
+ *   read as block 0, like the reference's safe_block_tables); a context
+ *   longer than the table covers is truncated to bt_width*block_size tokens
+ *   context_lens [B] int32 (0 -> out = 0)
+ *   scale: softmax scale applied to q.k in fp32 (1/sqrt(D) for Qwen3)
+ *   workspace: >= vj_paged_decode_workspace_size(B, Hq, D, max_chunks) bytes,
+ *   16-byte aligned; max_chunks bounds the split count (0 -> default 4096).
+ * ------------------------------------------------------------------------- */
+VJ_API size_t vj_paged_decode_workspace_size(int32_t batch, int32_t num_q_heads,
+                                      int32_t head_dim, int32_t max_chunks);
+
+VJ_API vj_status vj_paged_decode(
+    const void *q, const void *k_cache, const void *v_cache,
+    const int32_t *block_tables, const int32_t *context_lens, void *out,
+    int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+    int64_t num_blocks, int32_t block_size, int32_t bt_width, int32_t bt_stride,
+    int64_t stride_block, int64_t stride_token, int64_t stride_head,
+    float scale, int32_t max_chunks, void *workspace, size_t workspace_bytes,
+    cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VJATTN_H_ */

@@ -1,0 +1,103 @@
+"""Oracle for K3: q/k RMSNorm + RoPE + KV-slot scatter (test infrastructure).
+
+Follows vllm-jax vllm/model/qwen3.py:
+  :286-296  q = q_norm(q_proj(x)); q = apply_rope(q, ...); same for k
+  :59-78    apply_rope: positions.astype(bf16); inv_freq in bf16; pairs
+            (x[0::2], x[1::2]); stack((x1*cos - x2*sin, x1*sin + x2*cos), -1)
+  :105-111  _update_kv_cache: flat_cache.at[0|1, slot].set(k|v, mode="drop")
+RMSNorm follows flax nnx.RMSNorm (flax 0.12.2, call sites qwen3.py:248-268):
+fp32 statistics, y = bf16(x * (rsqrt(mean(x^2) + eps) * scale)).
+
+Every step below is one IEEE fp32 (or fp64 where stated) operation followed
+by a bf16 round-to-nearest-even wherever jnp's result dtype is bf16, so the
+CUDA kernel can be compared bit for bit.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from .bf16 import bf16, bf16_from_f64
+
+
+def rope_inv_freq(rope_theta: float, head_dim: int = 128) -> np.ndarray:
+    """1.0 / (rope_theta ** (arange(0, D, 2, bf16) / D)) in bf16 (qwen3.py:63-64).
+
+    rope_theta is a weakly typed Python float, so jnp casts it to bf16 before
+    the power (1e6 -> 999424)."""
+    theta = float(bf16_from_f64(np.float64(rope_theta)))
+    e = np.arange(0, head_dim, 2, dtype=np.float64) / head_dim   # exact in bf16
+    p = bf16_from_f64(np.power(theta, e))
+    return bf16_from_f64(1.0 / p.astype(np.float64))
+
+
+def rope_cos_sin(positions: np.ndarray, rope_theta: float, head_dim: int = 128):
+    """bf16 cos/sin tables [T, D/2] (qwen3.py:62-67); trig in fp64, one bf16 rounding."""
+    pos = bf16(np.asarray(positions, dtype=np.int64).astype(np.float32))
+    inv = rope_inv_freq(rope_theta, head_dim)
+    freqs = bf16(pos[:, None] * inv[None, :])          # einsum("t,d->td") in bf16
+    f64 = freqs.astype(np.float64)
+    return bf16_from_f64(np.cos(f64)), bf16_from_f64(np.sin(f64))
+
+
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """flax RMSNorm over the last axis; x, w bf16-valued float32 -> bf16-valued float32."""
+    x = np.asarray(x, np.float32)
+    ss = np.sum(x.astype(np.float64) ** 2, axis=-1, keepdims=True)
+    ms = np.float32(ss.astype(np.float32)) / np.float32(x.shape[-1])
+    inv = np.float32(1.0) / np.sqrt((ms + np.float32(eps)).astype(np.float32))
+    mul = (inv.astype(np.float32) * np.asarray(w, np.float32)).astype(np.float32)
+    return bf16((x * mul).astype(np.float32))
+
+
+def apply_rope(x: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
+    """Interleaved-pair RoPE of qwen3.py:69-75, bf16 after every op. x [T, H, D]."""
+    x1 = x[..., 0::2]
+    x2 = x[..., 1::2]
+    c = cos[:, None, :]
+    s = sin[:, None, :]
+    a = bf16(x1 * c)
+    b = bf16(x2 * s)
+    d = bf16(x1 * s)
+    e = bf16(x2 * c)
+    out = np.empty_like(x)
+    out[..., 0::2] = bf16(a - b)
+    out[..., 1::2] = bf16(d + e)
+    return out
+
+
+def update_kv_cache(k_cache: np.ndarray, v_cache: np.ndarray, slot_mapping: np.ndarray,
+                    k: np.ndarray, v: np.ndarray, wrap_negative: bool = True) -> None:
+    """In-place _update_kv_cache (qwen3.py:105-111).
+
+    k_cache/v_cache: [num_blocks, block_size, Hkv, D]. JAX's .at[] normalises
+    negative indices (slot -1 -> last slot) before mode="drop" drops the rest;
+    duplicate slots keep the last write (all duplicates in the reference are
+    identical padded rows)."""
+    nb, bs = k_cache.shape[:2]
+    n = nb * bs
+    fk = k_cache.reshape(n, *k_cache.shape[2:])
+    fv = v_cache.reshape(n, *v_cache.shape[2:])
+    for t, s in enumerate(np.asarray(slot_mapping, dtype=np.int64)):
+        if s < 0 and wrap_negative:
+            s += n
+        if 0 <= s < n:
+            fk[s] = k[t]
+            fv[s] = v[t]
+
+
+def kv_store_qknorm_rope(q, k, v, q_norm_w, k_norm_w, positions, slot_mapping,
+                         k_cache, v_cache, eps=1e-6, rope_theta=1e6,
+                         norm=True, rope=True, wrap_negative=True):
+    """Oracle of vj_kv_store_qknorm_rope. Returns (q_out, k_out); updates caches."""
+    q = np.asarray(q, np.float32)
+    k = np.asarray(k, np.float32)
+    if norm:
+        q = rmsnorm(q, q_norm_w, eps)
+        k = rmsnorm(k, k_norm_w, eps)
+    if rope:
+        c, s = rope_cos_sin(positions, rope_theta, q.shape[-1])
+        q = apply_rope(q, c, s)
+        k = apply_rope(k, c, s)
+    update_kv_cache(k_cache, v_cache, slot_mapping, k, np.asarray(v, np.float32),
+                    wrap_negative)
+    return q, k

@@ -1,0 +1,63 @@
+"""The C-ABI library loads on CPU, exports every symbol include/vjattn.h declares,
+and rejects bad arguments before touching the GPU."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADERS = sorted((ROOT / "include").glob("*.h"))
+
+
+def _declared_symbols():
+    names = set()
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names.update(re.findall(r"\b(vj_\w+)\s*\(", text))
+    return sorted(names)
+
+
+def test_header_declares_entry_points():
+    syms = _declared_symbols()
+    for required in ("vj_kv_store_qknorm_rope", "vj_paged_decode", "vj_get_last_error"):
+        assert required in syms
+
+
+def test_library_exports_every_declared_symbol():
+    from vllm_b200 import _native
+    lib = _native.load()
+    for name in _declared_symbols():
+        assert hasattr(lib, name), f"libvjattn.so does not export {name}"
+        assert name in _native.PROTOTYPES, f"no ctypes prototype for {name}"
+
+
+def test_validation_without_gpu():
+    from vllm_b200 import _native
+    lib = _native.load()
+    assert lib.vj_version() >> 16 == 1
+    # head_dim 64 is rejected before any CUDA call
+    st = lib.vj_kv_store_qknorm_rope(None, 1, 1, None, None, None, 1, None, None, 16, 16,
+                                     4, 0, 2, 64, 4, 16, 4096, 256, 128, 1e-6, 1e6, 0, None)
+    assert st == _native.VJ_ERR_UNSUPPORTED
+    assert b"head_dim" in lib.vj_get_last_error()
+    st = lib.vj_paged_decode(1, 1, 1, 1, 1, 1, 2, 12, 8, 128, 10, 16, 4, 4, 16 * 1024, 1024,
+                             128, 0.1, 0, None, 0, None)
+    assert st == _native.VJ_ERR_INVALID_ARGUMENT
+    assert b"divisible" in lib.vj_get_last_error()
+    # workspace too small
+    st = lib.vj_paged_decode(1, 1, 1, 1, 1, 1, 2, 32, 8, 128, 10, 16, 4, 4, 16 * 1024, 1024,
+                             128, 0.1, 0, 16, 8, None)
+    assert st == _native.VJ_ERR_WORKSPACE
+    assert lib.vj_paged_decode_workspace_size(256, 32, 128, 0) > 0
+    assert lib.vj_paged_decode_workspace_size(256, 32, 64, 0) == 0
+
+
+def test_no_cpu_fallback_for_cpu_tensors():
+    torch = pytest.importorskip("torch")
+    from vllm_b200.kernels.decode_paged_attention import paged_decode
+    q = torch.zeros(1, 32, 128, dtype=torch.bfloat16)
+    cache = torch.zeros(2, 4, 16, 8, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        paged_decode(q, cache, torch.zeros(1, 4, dtype=torch.int32),
+                     torch.ones(1, dtype=torch.int32))

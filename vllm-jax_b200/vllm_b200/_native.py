@@ -1,0 +1,84 @@
+"""ctypes binding of libvjattn.so, the sm_100a kernel library.
+
+There is no fallback: if the library is missing or fails to load, every op
+raises. The C prototypes mirror include/vjattn.h one to one.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+_LIB_PATH = Path(__file__).resolve().parent / "libvjattn.so"
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+c_int, c_i32, c_i64, c_f32, c_sz, c_vp = (ctypes.c_int, ctypes.c_int32, ctypes.c_int64,
+                                         ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p)
+
+# name -> (restype, argtypes); must match include/vjattn.h
+PROTOTYPES: dict[str, tuple] = {
+    "vj_get_last_error": (ctypes.c_char_p, []),
+    "vj_version": (c_int, []),
+    "vj_kv_store_qknorm_rope": (c_int, [
+        c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,   # q,k,v, qw,kw, positions, slots
+        c_vp, c_vp, c_vp, c_vp,                     # q_out, k_out, k_cache, v_cache
+        c_i64, c_i32, c_i32, c_i32, c_i64, c_i32,   # T, Hq, Hkv, D, nb, bs
+        c_i64, c_i64, c_i64,                        # strides (block, token, head)
+        c_f32, c_f32, c_i32, c_vp]),                # eps, theta, flags, stream
+    "vj_paged_decode_workspace_size": (c_sz, [c_i32, c_i32, c_i32, c_i32]),
+    "vj_paged_decode": (c_int, [
+        c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,         # q, k_cache, v_cache, bt, lens, out
+        c_i32, c_i32, c_i32, c_i32, c_i64, c_i32,   # B, Hq, Hkv, D, nb, bs
+        c_i32, c_i32,                               # bt_width, bt_stride
+        c_i64, c_i64, c_i64,                        # strides
+        c_f32, c_i32, c_vp, c_sz, c_vp]),           # scale, max_chunks, ws, ws_bytes, stream
+}
+
+# vj_status codes (include/vjattn.h)
+VJ_OK, VJ_ERR_INVALID_ARGUMENT, VJ_ERR_UNSUPPORTED, VJ_ERR_WORKSPACE, VJ_ERR_CUDA = range(5)
+VJ_KV_NORM, VJ_KV_ROPE, VJ_KV_WRAP_NEGATIVE = 1, 2, 4
+
+
+class VJError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"[vj_status {status}] {msg}")
+        self.status = status
+
+
+def lib_path() -> Path:
+    return Path(os.environ.get("VJATTN_LIB", _LIB_PATH))
+
+
+def load() -> ctypes.CDLL:
+    """Load libvjattn.so (once) and bind every prototype; raise if absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            path = lib_path()
+            if not path.exists():
+                raise RuntimeError(
+                    f"{path} not found: build it with `python -m vllm_b200.build` "
+                    "(there is no CPU fallback)")
+            lib = ctypes.CDLL(str(path))
+            for name, (res, args) in PROTOTYPES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def check(status: int) -> None:
+    if status != VJ_OK:
+        msg = load().vj_get_last_error().decode(errors="replace")
+        if status == VJ_ERR_INVALID_ARGUMENT:
+            raise ValueError(f"[vj_status {status}] {msg}")
+        raise VJError(status, msg)
+
+
+def call(name: str, *args) -> None:
+    check(getattr(load(), name)(*args))

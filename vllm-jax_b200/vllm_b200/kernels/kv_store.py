@@ -1,0 +1,97 @@
+"""KV-slot scatter fused with Qwen3's per-head q/k RMSNorm and RoPE (K3).
+
+Torch-facing wrappers of vj_kv_store_qknorm_rope. They replace, in vllm-jax:
+  vllm/model/qwen3.py:105-111  _update_kv_cache(kv_cache, slot_mapping, k, v)
+  vllm/model/qwen3.py:286-296  q_norm/k_norm + apply_rope (:59-78)
+The KV cache is updated IN PLACE (the reference's XLA scatter into a
+non-donated buffer copies the whole pool every layer).
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import _native
+from ._util import ptr, require_cuda, require_dtype, stream_ptr
+
+
+def _cache_views(kv_cache: torch.Tensor):
+    """kv_cache (2, num_blocks, block_size, Hkv, D) -> (k, v, nb, bs, strides)."""
+    if kv_cache.dim() != 5 or kv_cache.shape[0] != 2:
+        raise ValueError("kv_cache must have shape (2, num_blocks, block_size, Hkv, D); "
+                         f"got {tuple(kv_cache.shape)}")
+    require_dtype(kv_cache, torch.bfloat16, "kv_cache")
+    k, v = kv_cache[0], kv_cache[1]
+    if k.stride(-1) != 1:
+        raise ValueError("kv_cache head_dim must be contiguous")
+    nb, bs = k.shape[0], k.shape[1]
+    return k, v, nb, bs, (k.stride(0), k.stride(1), k.stride(2))
+
+
+def kv_store_qknorm_rope(q: torch.Tensor | None, k: torch.Tensor, v: torch.Tensor,
+                         kv_cache: torch.Tensor, slot_mapping: torch.Tensor,
+                         positions: torch.Tensor | None = None,
+                         q_norm_weight: torch.Tensor | None = None,
+                         k_norm_weight: torch.Tensor | None = None, *,
+                         eps: float = 1e-6, rope_theta: float = 1e6,
+                         norm: bool = True, rope: bool = True,
+                         wrap_negative_slots: bool = True,
+                         q_out: torch.Tensor | None = None,
+                         return_k: bool = False):
+    """One launch: q_out = rope(norm(q)), cache[slot] = (rope(norm(k)), v).
+
+    q [T, Hq, D] (or None), k/v [T, Hkv, D] bf16; slot_mapping/positions [T]
+    int32. Returns q_out (and k_out if return_k)."""
+    dev = require_cuda(k, v, kv_cache, slot_mapping)
+    kc, vc, nb, bs, (sb, st, sh) = _cache_views(kv_cache)
+    T, Hkv, D = k.shape
+    if v.shape != k.shape:
+        raise ValueError(f"k and v must have the same shape. Got {tuple(k.shape)} and {tuple(v.shape)}")
+    for name, t in (("k", k), ("v", v)):
+        require_dtype(t, torch.bfloat16, name)
+        if not t.is_contiguous():
+            raise ValueError(f"`{name}` must be contiguous")
+    require_dtype(slot_mapping, torch.int32, "slot_mapping")
+    if slot_mapping.shape != (T,):
+        raise ValueError("slot_mapping must have shape [num_tokens]")
+    Hq = 0
+    if q is not None:
+        require_dtype(q, torch.bfloat16, "q")
+        if q.dim() != 3 or q.shape[0] != T or q.shape[2] != D or not q.is_contiguous():
+            raise ValueError("q must be a contiguous [num_tokens, Hq, head_dim] tensor")
+        Hq = q.shape[1]
+        if q_out is None:
+            q_out = torch.empty_like(q)
+    if kc.shape[2] != Hkv or kc.shape[3] != D:
+        raise ValueError("kv_cache heads/head_dim do not match k")
+    flags = 0
+    if norm:
+        flags |= _native.VJ_KV_NORM
+        if k_norm_weight is None or (q is not None and q_norm_weight is None):
+            raise ValueError("norm=True needs q_norm_weight and k_norm_weight")
+    if rope:
+        flags |= _native.VJ_KV_ROPE
+        if positions is None:
+            raise ValueError("rope=True needs positions")
+        require_dtype(positions, torch.int32, "positions")
+    if wrap_negative_slots:
+        flags |= _native.VJ_KV_WRAP_NEGATIVE
+    k_out = torch.empty_like(k) if return_k else None
+    _native.call("vj_kv_store_qknorm_rope",
+                 ptr(q), k.data_ptr(), v.data_ptr(), ptr(q_norm_weight if norm else None),
+                 ptr(k_norm_weight if norm else None), ptr(positions if rope else None),
+                 slot_mapping.data_ptr(), ptr(q_out), ptr(k_out), kc.data_ptr(), vc.data_ptr(),
+                 T, Hq, Hkv, D, nb, bs, sb, st, sh, float(eps), float(rope_theta), flags,
+                 stream_ptr(dev))
+    if return_k:
+        return q_out, k_out
+    return q_out
+
+
+def update_kv_cache(kv_cache: torch.Tensor, slot_mapping: torch.Tensor, k: torch.Tensor,
+                    v: torch.Tensor) -> torch.Tensor:
+    """Drop-in for vllm/model/qwen3.py:105-111 `_update_kv_cache` (in place).
+
+    Slots are flat (block * block_size + offset); slot -1 wraps to the last
+    slot like JAX's .at[] with mode="drop"; other out-of-range slots drop."""
+    kv_store_qknorm_rope(None, k, v, kv_cache, slot_mapping, norm=False, rope=False)
+    return kv_cache
