@@ -47,8 +47,8 @@ C2 = dict(num_seqs=64, num_q_heads=32, num_kv_heads=8, head_dim=128, block_size=
 
 def c3_lengths(cfg=C3) -> np.ndarray:
     rng = np.random.default_rng(cfg["seed"])
-    u = rng.uniform(math.log(cfg["ctx_min"]), math.log(cfg["ctx_max"]), cfg["batch"])
-    return np.round(np.exp(u)).astype(np.int32)
+    u = rng.uniform(math.log(cfg["ctx_min"]), math.log(cfg["ctx_max"]), 256)
+    return np.round(np.exp(u)).astype(np.int32)[:cfg["batch"]]
 
 
 def c3_block_tables(lens: np.ndarray, cfg=C3) -> np.ndarray:
@@ -374,7 +374,15 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--ref-budget", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="profiling only: first B sequences of the C3 batch")
+    ap.add_argument("--pool-blocks", type=int, default=None,
+                    help="profiling only: KV pool size in blocks")
     args = ap.parse_args()
+    if args.batch is not None:
+        C3["batch"] = args.batch
+    if args.pool_blocks is not None:
+        C3["pool_blocks"] = args.pool_blocks
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -24,7 +24,7 @@ def rope_inv_freq(rope_theta: float, head_dim: int = 128) -> np.ndarray:
 
     rope_theta is a weakly typed Python float, so jnp casts it to bf16 before
     the power (1e6 -> 999424)."""
-    theta = float(bf16_from_f64(np.float64(rope_theta)))
+    theta = float(bf16_from_f64(np.array([rope_theta], np.float64))[0])
     e = np.arange(0, head_dim, 2, dtype=np.float64) / head_dim   # exact in bf16
     p = bf16_from_f64(np.power(theta, e))
     return bf16_from_f64(1.0 / p.astype(np.float64))
