@@ -122,6 +122,35 @@ VJ_API vj_status vj_paged_decode(
     float scale, int32_t max_chunks, void *workspace, size_t workspace_bytes,
     cudaStream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * K1: varlen paged prefill attention (causal), tcgen05/TMEM tiles fed by TMA.
+ * Replaces vllm/kernels/prefill_paged_attention.py:407-453
+ * (prefill_paged_attention) incl. the Q gather (:227-239), split merge
+ * (:364-376) and scatter to packed order (:384-388).
+ *
+ *   q [num_tokens, Hq, D] bf16 packed; sequence s owns rows
+ *   [cu_seqlens_q[s], cu_seqlens_q[s+1]); out has the same shape, rows past
+ *   cu_seqlens_q[num_seqs] are written as 0
+ *   context_lens [num_seqs] int32 = cached prefix + new tokens (keys already
+ *   in the pool), or NULL when keys == new tokens (the reference's case)
+ *   new token i of sequence s sits at position context_len - n_s + i and
+ *   attends to keys [0, that position]
+ *   block_tables [num_seqs, bt_width] int32 (row stride bt_stride)
+ *   max_seqlen_q: bound on new tokens per sequence (sizes the grid; <= 0 ->
+ *   num_tokens), like the reference's static max_seqlen_bucket
+ *   error_flag: device int32, set to 1 if a pipeline wait timed out
+ * Query heads per KV head must divide 128; head_dim 128; block_size % 16 == 0.
+ * ------------------------------------------------------------------------- */
+VJ_API vj_status vj_paged_prefill(
+    const void *q, const void *k_cache, const void *v_cache,
+    const int32_t *block_tables, const int32_t *cu_seqlens_q,
+    const int32_t *context_lens, void *out, int64_t num_tokens,
+    int32_t num_seqs, int32_t num_q_heads, int32_t num_kv_heads,
+    int32_t head_dim, int64_t num_blocks, int32_t block_size, int32_t bt_width,
+    int32_t bt_stride, int64_t stride_block, int64_t stride_token,
+    int64_t stride_head, int32_t max_seqlen_q, float scale,
+    int32_t *error_flag, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

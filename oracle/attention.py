@@ -42,11 +42,11 @@ def decode_attention(q, k_cache, v_cache, block_tables, context_lens, scale):
         k = gather_pages(k_cache, block_tables[b], L)      # [L, Hkv, D]
         v = gather_pages(v_cache, block_tables[b], L)
         qh = q[b].reshape(Hkv, g, D)
-        s = np.einsum("kgd,skd->kgs", qh, k, dtype=np.float32) * np.float32(scale)
+        s = np.matmul(qh, k.transpose(1, 2, 0)) * np.float32(scale)     # [Hkv, g, L]
         s = s - s.max(axis=-1, keepdims=True)
         p = np.exp(s, dtype=np.float32)
         p /= p.sum(axis=-1, keepdims=True)
-        o = np.einsum("kgs,skd->kgd", p, v, dtype=np.float32)
+        o = np.matmul(p, v.transpose(1, 0, 2))                          # [Hkv, g, D]
         out[b] = o.reshape(Hq, D)
     return bf16(out)
 
@@ -73,14 +73,16 @@ def prefill_attention(q, k_cache, v_cache, block_tables, cu_seqlens_q, seq_lens_
         p0 = Lk - n
         k = gather_pages(k_cache, block_tables[s_], Lk)
         v = gather_pages(v_cache, block_tables[s_], Lk)
-        qs = q[q0:q1].reshape(n, Hkv, g, D)
-        sc = np.einsum("nkgd,skd->kgns", qs, k, dtype=np.float32) * np.float32(scale)
+        qs = q[q0:q1].reshape(n, Hkv, g, D).transpose(1, 2, 0, 3)      # [Hkv, g, n, D]
+        kt = np.ascontiguousarray(k.transpose(1, 2, 0))                 # [Hkv, D, Lk]
+        vt = np.ascontiguousarray(v.transpose(1, 0, 2))                 # [Hkv, Lk, D]
+        sc = np.matmul(qs, kt[:, None]) * np.float32(scale)             # [Hkv, g, n, Lk]
         qpos = p0 + np.arange(n)
-        mask = np.arange(Lk)[None, :] <= qpos[:, None]          # [n, Lk]
+        mask = np.arange(Lk)[None, :] <= qpos[:, None]                  # [n, Lk]
         sc = np.where(mask[None, None], sc, -np.inf)
         sc = sc - sc.max(axis=-1, keepdims=True)
         p = np.exp(sc, dtype=np.float32)
         p /= p.sum(axis=-1, keepdims=True)
-        o = np.einsum("kgns,skd->nkgd", p, v, dtype=np.float32)
-        out[q0:q1] = o.reshape(n, Hq, D)
+        o = np.matmul(p, vt[:, None])                                   # [Hkv, g, n, D]
+        out[q0:q1] = o.transpose(2, 0, 1, 3).reshape(n, Hq, D)
     return bf16(out)
