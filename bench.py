@@ -63,6 +63,32 @@ def c3_block_tables(lens: np.ndarray, cfg=C3) -> np.ndarray:
     return bt
 
 
+def c2_batch(cfg=C2):
+    """C2: per-sequence new-token counts, cached prefixes and block tables."""
+    rng = np.random.default_rng(cfg["seed"])
+    S = cfg["num_seqs"]
+    new = rng.integers(cfg["new_min"], cfg["new_max"] + 1, S).astype(np.int32)
+    pre = rng.integers(cfg["prefix_min"], cfg["prefix_max"] + 1, S).astype(np.int32)
+    ctx = new + pre
+    bs = cfg["block_size"]
+    perm = rng.permutation(cfg["pool_blocks"]).astype(np.int32)
+    width = int(((ctx + bs - 1) // bs).max())
+    bt = np.full((S, width), -1, np.int32)
+    used = 0
+    for s_, c in enumerate(ctx):
+        k = (int(c) + bs - 1) // bs
+        bt[s_, :k] = perm[used:used + k]
+        used += k
+    return new, pre, bt
+
+
+def prefill_flops(new: np.ndarray, pre: np.ndarray, hq: int, d: int = 128) -> float:
+    """Causal-pair FLOPs: 4*Hq*D*(n*p + n(n+1)/2) per sequence (QK^T and PV)."""
+    n = new.astype(np.float64)
+    p = pre.astype(np.float64)
+    return float((4.0 * hq * d * (n * p + n * (n + 1) / 2)).sum())
+
+
 def decode_bytes(lens: np.ndarray, hkv: int, hq: int, d: int = 128, bs: int = 16) -> int:
     """Algorithmic HBM bytes of one decode call: K+V rows of every context token,
     q in + out, the used block-table entries and the lengths."""
@@ -305,7 +331,9 @@ def run_ours(args, rank, world, local_rank):
                      "frac": round(achieved / peaks["hbm_gbs"], 4),
                      "peak_source": f"{peak_src} hbm_gbs",
                      "kernel": "vj_paged_decode (plan + chunk + combine launches)",
-                     "traffic": DECODE_TRAFFIC_PER_LAUNCH if world == 1 else None},
+                     "traffic": decode_traffic(int(lens.sum())) if world == 1 else None,
+                     "traffic_source": "ncu dram bytes of a 48-sequence C3 capture, scaled "
+                                       "by context tokens"},
         "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": h_out.numel() * 2},
         "gpu_launches": 3 * args.steps,
@@ -318,9 +346,184 @@ def run_ours(args, rank, world, local_rank):
         pool.terminate()
 
 
-# DRAM bytes (read + write) of one full C3 vj_paged_decode call on one GPU,
-# from the ncu capture summarised in profiles/ (None until captured).
-DECODE_TRAFFIC_PER_LAUNCH = None
+def _cpu_prefill_seq(args):
+    n, p, hkv, g, seed = args
+    from oracle import attention as oatt
+    rng = np.random.default_rng(seed)
+    bs, d = 16, 128
+    L = n + p
+    npg = (L + bs - 1) // bs
+    kc = rng.standard_normal((npg, bs, hkv, d), dtype=np.float32)
+    vc = rng.standard_normal((npg, bs, hkv, d), dtype=np.float32)
+    q = rng.standard_normal((n, hkv * g, d), dtype=np.float32)
+    bt = np.arange(npg, dtype=np.int32)[None]
+    t0 = time.perf_counter()
+    oatt.prefill_attention(q, kc, vc, bt, np.array([0, n], np.int32), np.array([L], np.int32),
+                           1 / math.sqrt(d))
+    return time.perf_counter() - t0
+
+
+def cpu_prefill_baseline(new, pre, hkv, hq, budget_s, pool) -> dict:
+    """Oracle prefill on a seeded subsample of C2 sequences (shortest first so the
+    bounded sample covers several sequences), all host cores."""
+    order = np.argsort(new + pre)
+    cores = pool._processes if pool is not None else 1
+    done, sample, t_cpu = 0, [], 0.0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s and done < len(order):
+        idx = order[done:done + cores]
+        done += len(idx)
+        args = [(int(new[i]), int(pre[i]), hkv, hq // hkv, int(i)) for i in idx]
+        times = (pool.map(_cpu_prefill_seq, args) if pool is not None
+                 else [_cpu_prefill_seq(a) for a in args])
+        t_cpu += float(sum(times))
+        sample.extend(int(i) for i in idx)
+    fl = prefill_flops(new[sample], pre[sample], hq)
+    return {"value": fl / (t_cpu / cores) / 1e12, "unit": "TFLOP/s", "cores": cores,
+            "kind": "port",
+            "sample": f"{len(sample)} of {len(new)} C2 sequences ({int(new[sample].sum())} new "
+                      f"tokens) through the numpy oracle (oracle/attention.py:prefill_attention),"
+                      f" one sequence per process; {t_cpu:.1f} s of compute over {cores} "
+                      f"processes"}
+
+
+def run_prefill(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from vllm_b200.kernels.prefill_paged_attention import paged_prefill, pipeline_error
+
+    cfg = C2
+    pool = make_pool() if (rank == 0 and not args.no_cpu_baseline) else None
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    hkv_all, hq_all, D = cfg["num_kv_heads"], cfg["num_q_heads"], cfg["head_dim"]
+    if hkv_all % world:
+        raise SystemExit(f"--gpus {world} must divide {hkv_all} KV heads")
+    hkv, hq = hkv_all // world, hq_all // world
+    if args.batch is not None:
+        cfg["num_seqs"] = args.batch
+    if args.pool_blocks is not None:
+        cfg["pool_blocks"] = args.pool_blocks
+    new, pre, bt = c2_batch(cfg)
+    nb, bs = cfg["pool_blocks"], cfg["block_size"]
+    T = int(new.sum())
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2000 + rank)
+    kv_cache = torch.empty((2, nb, bs, hkv, D), dtype=torch.bfloat16, device=dev)
+    for i in range(2):
+        for c in range(0, nb, 20000):
+            kv_cache[i, c:c + 20000].normal_(generator=gen)
+    q = torch.randn((T, hq, D), generator=gen, device=dev).to(torch.bfloat16)
+    cu = np.concatenate([[0], np.cumsum(new)]).astype(np.int32)
+    ctx = (new + pre).astype(np.int32)
+    d_bt, d_cu, d_ctx = (torch.from_numpy(x).to(dev) for x in (bt, cu, ctx))
+    out = torch.empty_like(q)
+    maxq = int(new.max())
+
+    def step():
+        paged_prefill(q, kv_cache, d_bt, d_cu, d_ctx, max_seqlen_q=maxq, out=out)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if pipeline_error(dev):
+        raise SystemExit("prefill pipeline wait timed out")
+    if world > 1:
+        dist.barrier()
+    stream = torch.cuda.current_stream(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    t0e, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        t0e.record(stream)
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            step()
+            ev[i][1].record(stream)
+        t1e.record(stream)
+        torch.cuda.synchronize()
+    total_ms = t0e.elapsed_time(t1e)
+    per_launch_ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
+
+    h_q = q.cpu().pin_memory()
+    h_bt, h_cu, h_ctx = (torch.from_numpy(x).pin_memory() for x in (bt, cu, ctx))
+    h_out = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    e_q, e_bt, e_cu, e_ctx = (torch.empty_like(x) for x in (q, d_bt, d_cu, d_ctx))
+
+    def e2e_step():
+        e_q.copy_(h_q, non_blocking=True)
+        e_bt.copy_(h_bt, non_blocking=True)
+        e_cu.copy_(h_cu, non_blocking=True)
+        e_ctx.copy_(h_ctx, non_blocking=True)
+        paged_prefill(e_q, kv_cache, e_bt, e_cu, e_ctx, max_seqlen_q=maxq, out=out)
+        h_out.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    t = torch.tensor([total_ms, per_launch_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, per_launch_ms, e2e_ms = t.tolist()
+    if rank != 0:
+        return
+    fl_all = prefill_flops(new, pre, hq_all)
+    fl_rank = prefill_flops(new, pre, hq)
+    value = fl_all * args.steps / (total_ms / 1e3) / 1e12
+    peaks, src = load_peaks()
+    achieved = fl_rank / (per_launch_ms / 1e3) / 1e12
+    cpu = (cpu_prefill_baseline(new, pre, hkv_all, hq_all, args.cpu_budget, pool)
+           if pool is not None and world == 1 else None)
+    line = {
+        "metric": "paged-prefill TFLOP/s (C2: Qwen3-8B heads, 64 seqs, new U[128,4096], "
+                  "prefix U[0,2048], causal)",
+        "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(total_ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded C2 lengths/prefixes/tables; q,K,V ~ N(0,1) bf16)",
+        "config": {"workload": "C2 paged prefill attention", "num_seqs": len(new),
+                   "new_tokens": T, "prefix_tokens": int(pre.sum()), "num_q_heads": hq_all,
+                   "num_kv_heads": hkv_all, "head_dim": D, "block_size": bs, "pool_blocks": nb,
+                   "parallelism": f"tp{world} by KV head" if world > 1 else "single GPU",
+                   "l2": f"inputs larger than L2 (q {T * hq_all * D * 2 / 1e9:.2f} GB)"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1),
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": round(achieved / peaks["bf16_tflops"], 4),
+                     "peak_source": f"{src} bf16_tflops (burst)",
+                     "kernel": "vj_paged_prefill (prefill_kernel + zero-tail)",
+                     "traffic": None},
+        "e2e": {"value": round(fl_all * args.steps / (e2e_ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": h_q.numel() * 2 + (h_bt.numel() + h_cu.numel() +
+                                                         h_ctx.numel()) * 4,
+                "d2h_bytes_per_step": h_out.numel() * 2},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk.summary(),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    if pool is not None:
+        pool.terminate()
+
+
+# ncu capture of decode_chunk_kernel on the first 48 C3 sequences (402,759
+# context tokens; profiles/decode_chunk_kernel_c3.md): dram read + write bytes.
+# DRAM traffic grows with the context tokens streamed, so a full C3 launch is
+# scaled by its context-token count.
+DECODE_PROFILE = {"ctx_tokens": 402_759, "dram_bytes": 1_651_773_000 + 38_666_240}
+
+
+def decode_traffic(ctx_tokens: int) -> int:
+    return int(DECODE_PROFILE["dram_bytes"] * ctx_tokens / DECODE_PROFILE["ctx_tokens"])
 
 
 # ---------------------------------------------------------------------------
@@ -370,7 +573,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--ref-budget", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -398,7 +601,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, rank, world, local_rank)
+        if args.workload == "prefill":
+            run_prefill(args, rank, world, local_rank)
+        else:
+            run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

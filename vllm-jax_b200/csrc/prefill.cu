@@ -11,14 +11,19 @@
 // One CTA = one 128-row Q tile of one (sequence, KV head): the rows pack the
 // GQA group, row r = (token r / g, head r % g), so each K/V byte loaded by TMA
 // feeds all g query heads. Keys stream in tiles of 128 (8 pages of 16).
+// Both GEMMs take their A operand from tensor memory, so shared memory only
+// feeds B (K or V) and the tensor pipe is not capped by smem bandwidth:
+//   TMEM columns [0,128) S0 | [128,256) S1 | [256,384) O | [384,448) Q
+//   P_j (bf16) overwrites the first 64 columns of S_(j&1) after softmax reads it.
 // Warp roles (192 threads):
-//   warps 0-3  softmax: one thread per row; reads S from TMEM, online
-//              softmax in fp32 (exp2), writes P (bf16) to shared memory,
-//              rescales O in TMEM only when the running max grows by more
-//              than 2^8 (exact: l and O always share the same reference max)
-//   warp 4     TMA producer: Q once, then K/V pages through a 2-stage ring
-//   warp 5     MMA issuer (one thread): S = Q K^T into a double-buffered TMEM
-//              accumulator, O += P V into a TMEM accumulator
+//   warps 0-3  softmax: one thread per row. Loads its Q row into TMEM once;
+//              per key tile reads S from TMEM, online softmax in fp32 (exp2),
+//              writes P back into TMEM, and rescales O in TMEM only when the
+//              running max grows by more than 2^8 (exact: l and O always
+//              share the same reference max)
+//   warp 4     TMA producer: K/V pages through a 3-stage ring
+//   warp 5     MMA issuer (one thread), in order QK_0, QK_1, PV_0, QK_2, PV_1
+//              ...: S_(j+1) is computed while softmax works on S_j
 // Tensor-core bound: FLOPs = 4 * Hq * D * (n*p + n(n+1)/2) per sequence.
 #include "../../include/vjattn.h"
 #include "vj_common.cuh"
@@ -36,18 +41,18 @@ constexpr int kPagesPerTile = kBN / kPageTok;
 constexpr int kThreads = 192;
 constexpr int kHalf = 128 * 128;   // bytes of a [128 rows x 64 bf16] swizzled half tile
 constexpr int kTile = 2 * kHalf;   // [128 x 128] bf16
-constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + kTile;
-constexpr int OFF_V = OFF_K + 2 * kTile;
-constexpr int OFF_P = OFF_V + 2 * kTile;
-constexpr int OFF_BAR = OFF_P + kTile;
+constexpr int kStages = 3;
+constexpr int OFF_K = 0;
+constexpr int OFF_V = OFF_K + kStages * kTile;
+constexpr int OFF_BAR = OFF_V + kStages * kTile;
+constexpr uint32_t TM_S = 0, TM_O = 256, TM_Q = 384;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct Bars {
   uint64_t q_full;
-  uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
-  uint64_t s_full[2], s_free[2];
+  uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
+  uint64_t s_full[2];
   uint64_t p_full, o_done;
   uint32_t tmem_base;
   int abort;
@@ -55,6 +60,7 @@ struct Bars {
 constexpr size_t kSmemBytes = 1024 + OFF_BAR + sizeof(Bars);
 
 struct PrefillArgs {
+  const __nv_bfloat16 *q;
   __nv_bfloat16 *out;
   const int32_t *bt;
   const int32_t *cu;
@@ -67,27 +73,36 @@ struct PrefillArgs {
   int *err;
 };
 
+// Token coordinate (flat pool token index of the page's first token) of page
+// grp*32 + lane of sequence s: one coalesced block-table read per 4 KV tiles.
+VJ_DEV int page_tok0(const PrefillArgs &a, const int32_t *row, int grp, int lane) {
+  const int page = grp * 32 + lane;
+  int blk = 0;
+  if (page < a.max_pages) {
+    blk = __ldg(row + page / a.pages_per_block);
+    if (blk < 0 || blk >= a.num_blocks) blk = 0;  // safe_block_tables
+  }
+  return blk * a.block_size + (page % a.pages_per_block) * kPageTok;
+}
+
+// Issue the 16 TMA boxes (8 pages x 2 dim halves) of one K or V tile; the
+// page coordinates live in the producer warp's lanes (tile jj of the group).
 VJ_DEV void load_kv_tile(const CUtensorMap *tm, uint8_t *dst, uint64_t *bar, const PrefillArgs &a,
-                         int s, int h, int j) {
-  const int32_t *row = a.bt + (size_t)s * a.bt_stride;
-#pragma unroll 1
+                         int h, int toks, int jj, int lane) {
+#pragma unroll
   for (int pg = 0; pg < kPagesPerTile; ++pg) {
-    const int page = j * kPagesPerTile + pg;
-    int blk = 0;
-    if (page < a.max_pages) {
-      blk = __ldg(row + page / a.pages_per_block);
-      if (blk < 0 || blk >= a.num_blocks) blk = 0;
+    const int tok0 = __shfl_sync(0xffffffffu, toks, jj * kPagesPerTile + pg);
+    if (lane == 0) {
+      const int c1 = a.head_major ? h : tok0, c2 = a.head_major ? tok0 : h;
+      tma_load_3d(dst + pg * (kPageTok * 128), tm, bar, 0, c1, c2);
+      tma_load_3d(dst + kHalf + pg * (kPageTok * 128), tm, bar, 64, c1, c2);
     }
-    const int tok0 = blk * a.block_size + (page % a.pages_per_block) * kPageTok;
-    const int c1 = a.head_major ? h : tok0, c2 = a.head_major ? tok0 : h;
-    tma_load_3d(dst + pg * (kPageTok * 128), tm, bar, 0, c1, c2);
-    tma_load_3d(dst + kHalf + pg * (kPageTok * 128), tm, bar, 64, c1, c2);
   }
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-prefill_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-               const __grid_constant__ CUtensorMap tmv, PrefillArgs a) {
+prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+               PrefillArgs a) {
   const int s = blockIdx.z, h = blockIdx.y;
   const int m = gridDim.x - 1 - blockIdx.x;  // longest tiles first
   const int q0 = __ldg(a.cu + s);
@@ -108,15 +123,14 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    mbar_init(&bar.q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    mbar_init(&bar.q_full, 128);
+    for (int i = 0; i < kStages; ++i) {
       mbar_init(&bar.k_full[i], 1);
       mbar_init(&bar.k_empty[i], 1);
       mbar_init(&bar.v_full[i], 1);
       mbar_init(&bar.v_empty[i], 1);
-      mbar_init(&bar.s_full[i], 1);
-      mbar_init(&bar.s_free[i], 128);
     }
+    for (int i = 0; i < 2; ++i) mbar_init(&bar.s_full[i], 1);
     mbar_init(&bar.p_full, 128);
     mbar_init(&bar.o_done, 1);
     bar.abort = 0;
@@ -131,66 +145,74 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
 
   if (warp == 4) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      tma_prefetch_desc(&tmq); tma_prefetch_desc(&tmk); tma_prefetch_desc(&tmv);
-      mbar_arrive_expect_tx(&bar.q_full, kTile);
-      tma_load_3d(smem + OFF_Q, &tmq, &bar.q_full, 0, h * a.g, q0 + tq0);
-      tma_load_3d(smem + OFF_Q + kHalf, &tmq, &bar.q_full, 64, h * a.g, q0 + tq0);
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int st = j & 1;
-        if (j >= 2) ok = mbar_wait(&bar.k_empty[st], ((j - 2) >> 1) & 1);
-        if (!ok) break;
-        mbar_arrive_expect_tx(&bar.k_full[st], kTile);
-        load_kv_tile(&tmk, smem + OFF_K + st * kTile, &bar.k_full[st], a, s, h, j);
-        if (j >= 2) ok = mbar_wait(&bar.v_empty[st], ((j - 2) >> 1) & 1);
-        if (!ok) break;
-        mbar_arrive_expect_tx(&bar.v_full[st], kTile);
-        load_kv_tile(&tmv, smem + OFF_V + st * kTile, &bar.v_full[st], a, s, h, j);
+    // whole warp: lanes hold page coordinates, lane 0 issues the copies
+    const int32_t *row = a.bt + (size_t)s * a.bt_stride;
+    int cur = page_tok0(a, row, 0, lane);
+    int nxt = nkv > 4 ? page_tok0(a, row, 1, lane) : 0;
+    if (lane == 0) { tma_prefetch_desc(&tmk); tma_prefetch_desc(&tmv); }
+    for (int j = 0; j < nkv && ok; ++j) {
+      const int st = j % kStages, jj = j & 3;
+      const uint32_t use = j / kStages;  // how many times this stage was filled before
+      if (jj == 0 && j > 0) {
+        cur = nxt;
+        nxt = j + 4 < nkv ? page_tok0(a, row, (j >> 2) + 1, lane) : 0;
       }
+      if (use > 0) ok = mbar_wait(&bar.k_empty[st], (use - 1) & 1);
+      if (!ok) break;
+      if (lane == 0) mbar_arrive_expect_tx(&bar.k_full[st], kTile);
+      load_kv_tile(&tmk, smem + OFF_K + st * kTile, &bar.k_full[st], a, h, cur, jj, lane);
+      if (use > 0) ok = mbar_wait(&bar.v_empty[st], (use - 1) & 1);
+      if (!ok) break;
+      if (lane == 0) mbar_arrive_expect_tx(&bar.v_full[st], kTile);
+      load_kv_tile(&tmv, smem + OFF_V + st * kTile, &bar.v_full[st], a, h, cur, jj, lane);
     }
   } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_qk = umma_idesc_bf16(kBM, kBN, false);
       constexpr uint32_t idesc_pv = umma_idesc_bf16(kBM, kD, true);
-      const uint32_t sq = smem_u32(smem + OFF_Q), sk = smem_u32(smem + OFF_K),
-                     sv = smem_u32(smem + OFF_V), sp = smem_u32(smem + OFF_P);
+      const uint32_t sk = smem_u32(smem + OFF_K), sv = smem_u32(smem + OFF_V);
+      auto issue_qk = [&](int j) -> bool {
+        const int st = j % kStages;
+        if (!mbar_wait(&bar.k_full[st], (j / kStages) & 1)) return false;
+        tc_fence_after();
+        const uint32_t kb = sk + st * kTile;
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          // A = Q (TMEM, 8 columns per 16 dims), B = K tile (K-major, swizzled)
+          umma_ts(tmem + TM_S + (j & 1) * kBN, tmem + TM_Q + kk * 8,
+                  umma_desc_sw128(kb + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024), idesc_qk,
+                  kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bar.s_full[j & 1]);
+        umma_commit(&bar.k_empty[st]);
+        return true;
+      };
       ok = mbar_wait(&bar.q_full, 0);
       tc_fence_after();
-      for (int j = 0; j <= nkv && ok; ++j) {
-        if (j < nkv) {
-          const int b = j & 1;
-          ok = mbar_wait(&bar.k_full[b], (j >> 1) & 1);
-          if (ok && j >= 2) ok = mbar_wait(&bar.s_free[b], ((j - 2) >> 1) & 1);
+      if (ok) ok = issue_qk(0);
+      for (int j = 0; j < nkv && ok; ++j) {
+        // S_(j+1) overwrites the buffer of P_(j-1); PV_(j-1) was issued
+        // before it and tcgen05 MMAs of one thread execute in issue order.
+        if (j + 1 < nkv) {
+          ok = issue_qk(j + 1);
           if (!ok) break;
-          tc_fence_after();
-          const uint32_t kb = sk + b * kTile;
-#pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-            umma_ss(tmem + b * kBN, umma_desc_sw128(sq + off, 16, 1024),
-                    umma_desc_sw128(kb + off, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(&bar.s_full[b]);
-          umma_commit(&bar.k_empty[b]);
         }
-        if (j >= 1) {
-          const int jj = j - 1, st = jj & 1;
-          ok = mbar_wait(&bar.p_full, jj & 1);
-          if (ok) ok = mbar_wait(&bar.v_full[st], (jj >> 1) & 1);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t vb = sv + st * kTile;
+        const int st = j % kStages;
+        ok = mbar_wait(&bar.p_full, j & 1);
+        if (ok) ok = mbar_wait(&bar.v_full[st], (j / kStages) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t vb = sv + st * kTile;
 #pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk) {
-            umma_ss(tmem + 2 * kBN,
-                    umma_desc_sw128(sp + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024),
-                    umma_desc_sw128(vb + kk * 2048, kHalf, 1024), idesc_pv,
-                    (jj > 0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(&bar.o_done);
-          umma_commit(&bar.v_empty[st]);
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          // A = P (TMEM, aliased on S_(j&1)), B = V tile (MN-major: keys x dims)
+          umma_ts(tmem + TM_O, tmem + TM_S + (j & 1) * kBN + kk * 8,
+                  umma_desc_sw128(vb + kk * 2048, kHalf, 1024), idesc_pv,
+                  (j > 0 || kk > 0) ? 1u : 0u);
         }
+        umma_commit(&bar.o_done);
+        umma_commit(&bar.v_empty[st]);
       }
     }
   } else {
@@ -199,7 +221,26 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
     const int tq = tq0 + r / a.g;
     const int qpos = p0 + tq;
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    uint8_t *sP = smem + OFF_P;
+    {
+      // this row of Q -> TMEM (two bf16 per column); rows past the tensor are 0
+      uint32_t qv[64];
+      const int64_t tok = (int64_t)q0 + tq;
+      if (tok < a.num_tokens) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(
+            a.q + (tok * a.Hq + (int64_t)h * a.g + (r % a.g)) * kD);
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const uint4 w = __ldg(src + c);
+          qv[4 * c] = w.x; qv[4 * c + 1] = w.y; qv[4 * c + 2] = w.z; qv[4 * c + 3] = w.w;
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) qv[c] = 0u;
+      }
+      tmem_st64_sync(tmem + lane_base + TM_Q, qv);
+      tc_fence_before();
+      mbar_arrive(&bar.q_full);
+    }
     float m_run = -INFINITY, l_run = 0.f;
     float sv[kBN];
     for (int j = 0; j < nkv; ++j) {
@@ -207,34 +248,30 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
       ok = mbar_wait(&bar.s_full[b], (j >> 1) & 1);
       if (!ok) break;
       tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        float t[32];
-        tmem_ld32(tmem + lane_base + b * kBN + c * 32, t);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = t[i];
-      }
-      tc_fence_before();
-      mbar_arrive(&bar.s_free[b]);
+      tmem_ld128(tmem + lane_base + TM_S + b * kBN, sv);
 
       const int kbase = j * kBN;
       const bool masked = kbase + kBN - 1 > qpos_min;
       float mx = -INFINITY;
+      if (masked) {
 #pragma unroll
-      for (int i = 0; i < kBN; ++i) {
-        float v = sv[i] * a.scale_log2;
-        if (masked && kbase + i > qpos) v = -INFINITY;
-        sv[i] = v;
-        mx = fmaxf(mx, v);
+        for (int i = 0; i < kBN; ++i) {
+          if (kbase + i > qpos) sv[i] = -INFINITY;
+          mx = fmaxf(mx, sv[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < kBN; ++i) mx = fmaxf(mx, sv[i]);
       }
-      const float m_new = fmaxf(m_run, mx);
+      // scores are raw q.k; the softmax scale (and log2 e) folds into one FFMA
+      const float m_new = fmaxf(m_run, mx * a.scale_log2);
       const bool need = j > 0 && (m_new - m_run > kRescaleThreshold);
       const float m_use = (j == 0 || need) ? m_new : m_run;
       const float corr = j == 0 ? 0.f : fast_exp2(m_run - m_use);
       float sum = 0.f;
 #pragma unroll
       for (int i = 0; i < kBN; ++i) {
-        sv[i] = fast_exp2(sv[i] - m_use);
+        sv[i] = fast_exp2(fmaf(sv[i], a.scale_log2, -m_use));
         sum += sv[i];
       }
       l_run = l_run * corr + sum;
@@ -248,7 +285,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
 #pragma unroll 1
           for (int c = 0; c < kD / 32; ++c) {
             float t[32];
-            const uint32_t ta = tmem + lane_base + 2 * kBN + c * 32;
+            const uint32_t ta = tmem + lane_base + TM_O + c * 32;
             tmem_ld32(ta, t);
 #pragma unroll
             for (int i = 0; i < 32; ++i) t[i] *= corr;
@@ -257,17 +294,13 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
           tmem_st_wait();
         }
       }
-      // P row r -> shared memory, K-major 128B-swizzled (two 64-key halves)
+      // P row r (bf16 pairs) -> TMEM over the first 64 columns of S_b
+      {
+        uint32_t pv[64];
 #pragma unroll
-      for (int c = 0; c < kBN / 8; ++c) {
-        uint4 w;
-        w.x = pack_bf16(sv[8 * c + 0], sv[8 * c + 1]);
-        w.y = pack_bf16(sv[8 * c + 2], sv[8 * c + 3]);
-        w.z = pack_bf16(sv[8 * c + 4], sv[8 * c + 5]);
-        w.w = pack_bf16(sv[8 * c + 6], sv[8 * c + 7]);
-        *reinterpret_cast<uint4 *>(sP + (c >> 3) * kHalf + sw128(r, c & 7)) = w;
+        for (int c = 0; c < 64; ++c) pv[c] = pack_bf16(sv[2 * c], sv[2 * c + 1]);
+        tmem_st64_sync(tmem + lane_base + TM_S + b * kBN, pv);
       }
-      fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&bar.p_full);
     }
@@ -282,7 +315,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
 #pragma unroll 1
       for (int c = 0; c < kD / 32; ++c) {
         float t[32];
-        tmem_ld32(tmem + lane_base + 2 * kBN + c * 32, t);
+        tmem_ld32(tmem + lane_base + TM_O + c * 32, t);
         if (valid) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
@@ -360,10 +393,8 @@ extern "C" vj_status vj_paged_prefill(
     return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_paged_prefill: null pointer");
   }
   const int tt = kBM / g;
-  CUtensorMap tmq, tmk, tmv;
-  int rc = encode_tmap_3d(&tmq, q, kD, num_q_heads, num_tokens, (uint64_t)kD * 2,
-                          (uint64_t)num_q_heads * kD * 2, 64, g, tt, true);
-  if (rc) return rc;
+  CUtensorMap tmk, tmv;
+  int rc = VJ_OK;
   const uint64_t ntok = (uint64_t)num_blocks * block_size;
   const bool head_major = stride_head < stride_token;
   for (int i = 0; i < 2; ++i) {
@@ -376,6 +407,7 @@ extern "C" vj_status vj_paged_prefill(
     if (rc) return rc;
   }
   PrefillArgs a;
+  a.q = static_cast<const __nv_bfloat16 *>(q);
   a.out = static_cast<__nv_bfloat16 *>(out);
   a.bt = block_tables;
   a.cu = cu_seqlens_q;
@@ -400,7 +432,7 @@ extern "C" vj_status vj_paged_prefill(
     cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)kSmemBytes);
     dim3 grid((unsigned)mtiles, num_kv_heads, num_seqs);
-    prefill_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tmq, tmk, tmv, a);
+    prefill_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tmk, tmv, a);
     rc = check_launch("vj_paged_prefill");
     if (rc) return rc;
   }
