@@ -8,22 +8,30 @@
 // prefix: new token i of sequence s sits at position ctx_s - n_s + i and
 // attends to keys [0, that position].
 //
-// One CTA = one 128-row Q tile of one (sequence, KV head): the rows pack the
-// GQA group, row r = (token r / g, head r % g), so each K/V byte loaded by TMA
-// feeds all g query heads. Keys stream in tiles of 128 (8 pages of 16).
-// Both GEMMs take their A operand from tensor memory, so shared memory only
-// feeds B (K or V) and the tensor pipe is not capped by smem bandwidth:
-//   TMEM columns [0,128) S0 | [128,256) S1 | [256,384) O | [384,448) Q
-//   P_j (bf16) overwrites the first 64 columns of S_(j&1) after softmax reads it.
-// Warp roles (192 threads):
-//   warps 0-3  softmax: one thread per row. Loads its Q row into TMEM once;
-//              per key tile reads S from TMEM, online softmax in fp32 (exp2),
-//              writes P back into TMEM, and rescales O in TMEM only when the
-//              running max grows by more than 2^8 (exact: l and O always
-//              share the same reference max)
-//   warp 4     TMA producer: K/V pages through a 3-stage ring
-//   warp 5     MMA issuer (one thread), in order QK_0, QK_1, PV_0, QK_2, PV_1
-//              ...: S_(j+1) is computed while softmax works on S_j
+// One CTA = two consecutive 128-row Q tiles (A, B) of one (sequence, KV
+// head). Rows pack the GQA group, row r = (token r / g, head r % g), so each
+// K/V byte loaded feeds all g query heads of 2 tiles: the paged K/V stream
+// (16 TMA boxes of 16 tokens x 64 dims per 128-key tile) is what bounds a
+// one-tile-per-CTA design, and sharing it between two tiles halves it.
+//
+//   TMEM columns: [0,128) S_A | [128,256) S_B | [256,384) O_A | [384,512) O_B
+//   P_X (bf16 pairs) overwrites the first 64 columns of S_X after softmax
+//   reads it; PV takes P straight from TMEM (A operand), V from smem.
+//   Shared memory: Q_A, Q_B (32 KB each), K ring 3 x 32 KB, V ring 2 x 32 KB,
+//   all 128-byte swizzled K-major / MN-major UMMA layouts written by TMA.
+//
+// Warp roles (352 threads):
+//   warps 0-3 / 4-7  softmax of tile A / B: one thread per row; per key tile
+//                    read S (128 fp32 columns) from TMEM, online softmax in
+//                    fp32 with exp2 (a fixed share on an FMA polynomial to
+//                    offload the MUFU unit), P back to TMEM; O is rescaled
+//                    in TMEM only when the running max grows by more than
+//                    2^8 (exact: l and O always share the same reference max)
+//   warp 8           TMA producer of K tiles (and Q once)
+//   warp 9           MMA issuer (one thread), order per key tile j:
+//                    PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1) -- the tensor
+//                    core works on one tile while softmax works on the other
+//   warp 10          TMA producer of V tiles
 // Tensor-core bound: FLOPs = 4 * Hq * D * (n*p + n(n+1)/2) per sequence.
 #include "../../include/vjattn.h"
 #include "vj_common.cuh"
@@ -38,29 +46,51 @@ constexpr int kBM = 128;   // rows per Q tile
 constexpr int kBN = 128;   // keys per KV tile
 constexpr int kPageTok = 16;
 constexpr int kPagesPerTile = kBN / kPageTok;
-constexpr int kThreads = 192;
+constexpr int kThreads = 352;
+constexpr int kWarpK = 8, kWarpMma = 9, kWarpV = 10;
 constexpr int kHalf = 128 * 128;   // bytes of a [128 rows x 64 bf16] swizzled half tile
 constexpr int kTile = 2 * kHalf;   // [128 x 128] bf16
-constexpr int kStages = 3;
-constexpr int OFF_K = 0;
-constexpr int OFF_V = OFF_K + kStages * kTile;
-constexpr int OFF_BAR = OFF_V + kStages * kTile;
-constexpr uint32_t TM_S = 0, TM_O = 256, TM_Q = 384;
-constexpr float kRescaleThreshold = 8.0f;  // log2 units
+constexpr int kKStages = 3, kVStages = 2;
+constexpr int OFF_Q = 0;                        // Q_A, Q_B
+constexpr int OFF_K = OFF_Q + 2 * kTile;
+constexpr int OFF_V = OFF_K + kKStages * kTile;
+constexpr int OFF_BAR = OFF_V + kVStages * kTile;
+constexpr uint32_t TM_S = 0, TM_O = 256;        // + tile * 128
+constexpr float kRescaleThreshold = 8.0f;       // log2 units
 constexpr float kLog2e = 1.4426950408889634f;
+
+// Softmax exponentials are split between the MUFU unit (ex2.approx) and a
+// cubic polynomial on the FMA pipe: with two Q tiles per key tile, MUFU work
+// equals the tensor-core time. Bit k of kEmuMask set -> columns i with
+// i % 8 == k use the polynomial. 2^f on [-0.5, 0.5] is approximated by a
+// cubic fitted for minimum relative error (max 2.1e-4, well below bf16's 2^-9
+// rounding of P).
+#ifndef VJ_PREFILL_EMU_MASK
+#define VJ_PREFILL_EMU_MASK 0x80
+#endif
+constexpr unsigned kEmuMask = VJ_PREFILL_EMU_MASK;
+constexpr float kP0 = 0.99995905f, kP1 = 0.69357258f, kP2 = 0.24221395f, kP3 = 0.05302752f;
+
+VJ_DEV float poly_exp2(float x) {
+  x = fmaxf(x, -125.f);                  // keeps the exponent field positive
+  const float t = x + 12582912.f;        // 1.5 * 2^23: round(x) lands in the low bits
+  const float n = t - 12582912.f;
+  const float f = x - n;                 // [-0.5, 0.5]
+  const float p = fmaf(fmaf(fmaf(kP3, f, kP2), f, kP1), f, kP0);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
 
 struct Bars {
   uint64_t q_full;
-  uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
-  uint64_t s_full[2];
-  uint64_t p_full, o_done;
+  uint64_t k_full[kKStages], k_empty[kKStages];
+  uint64_t v_full[kVStages], v_empty[kVStages];
+  uint64_t s_full[2], p_full[2], o_final[2];
   uint32_t tmem_base;
-  int abort;
 };
 constexpr size_t kSmemBytes = 1024 + OFF_BAR + sizeof(Bars);
+static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 struct PrefillArgs {
-  const __nv_bfloat16 *q;
   __nv_bfloat16 *out;
   const int32_t *bt;
   const int32_t *cu;
@@ -85,35 +115,53 @@ VJ_DEV int page_tok0(const PrefillArgs &a, const int32_t *row, int grp, int lane
   return blk * a.block_size + (page % a.pages_per_block) * kPageTok;
 }
 
-// Issue the 16 TMA boxes (8 pages x 2 dim halves) of one K or V tile; the
-// page coordinates live in the producer warp's lanes (tile jj of the group).
-VJ_DEV void load_kv_tile(const CUtensorMap *tm, uint8_t *dst, uint64_t *bar, const PrefillArgs &a,
-                         int h, int toks, int jj, int lane) {
+// Stream the K or V tiles of one work item through a ring of `stages`
+// buffers; the whole warp runs this (lanes hold page coordinates), lane 0
+// issues the copies. Returns false if a wait timed out.
+template <int kStagesT>
+VJ_DEV bool produce_kv(const CUtensorMap *tm, uint8_t *ring, uint64_t *full, uint64_t *empty,
+                       const PrefillArgs &a, int s, int h, int nkv, int lane) {
+  const int32_t *row = a.bt + (size_t)s * a.bt_stride;
+  int cur = page_tok0(a, row, 0, lane);
+  int nxt = nkv > 4 ? page_tok0(a, row, 1, lane) : 0;
+  for (int j = 0; j < nkv; ++j) {
+    const int st = j % kStagesT, jj = j & 3;
+    const int use = j / kStagesT;
+    if (jj == 0 && j > 0) {
+      cur = nxt;
+      nxt = j + 4 < nkv ? page_tok0(a, row, (j >> 2) + 1, lane) : 0;
+    }
+    bool ok = true;
+    if (use > 0) ok = mbar_wait(&empty[st], (use - 1) & 1);
+    if (!__all_sync(0xffffffffu, ok)) return false;
+    if (lane == 0) mbar_arrive_expect_tx(&full[st], kTile);
+    uint8_t *dst = ring + st * kTile;
 #pragma unroll
-  for (int pg = 0; pg < kPagesPerTile; ++pg) {
-    const int tok0 = __shfl_sync(0xffffffffu, toks, jj * kPagesPerTile + pg);
-    if (lane == 0) {
-      const int c1 = a.head_major ? h : tok0, c2 = a.head_major ? tok0 : h;
-      tma_load_3d(dst + pg * (kPageTok * 128), tm, bar, 0, c1, c2);
-      tma_load_3d(dst + kHalf + pg * (kPageTok * 128), tm, bar, 64, c1, c2);
+    for (int pg = 0; pg < kPagesPerTile; ++pg) {
+      const int tok0 = __shfl_sync(0xffffffffu, cur, jj * kPagesPerTile + pg);
+      if (lane == 0) {
+        const int c1 = a.head_major ? h : tok0, c2 = a.head_major ? tok0 : h;
+        tma_load_3d(dst + pg * (kPageTok * 128), tm, &full[st], 0, c1, c2);
+        tma_load_3d(dst + kHalf + pg * (kPageTok * 128), tm, &full[st], 64, c1, c2);
+      }
     }
   }
+  return true;
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-               PrefillArgs a) {
+prefill_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+               const __grid_constant__ CUtensorMap tmv, PrefillArgs a) {
   const int s = blockIdx.z, h = blockIdx.y;
-  const int m = gridDim.x - 1 - blockIdx.x;  // longest tiles first
+  const int m2 = gridDim.x - 1 - blockIdx.x;  // longest tile pairs first
   const int q0 = __ldg(a.cu + s);
   const int n = __ldg(a.cu + s + 1) - q0;
-  const int tq0 = m * a.tt;
+  const int tq0 = m2 * 2 * a.tt;               // first token of tile A
   if (tq0 >= n) return;  // whole CTA, before any barrier or TMEM use
   int ctx = a.ctx_lens ? __ldg(a.ctx_lens + s) : n;
   if (ctx < n) ctx = n;
   const int p0 = ctx - n;                          // cached prefix length
-  const int qpos_min = p0 + tq0;
-  const int kv_end = p0 + min(n, tq0 + a.tt);      // keys visible to the last row
+  const int kv_end = p0 + min(n, tq0 + 2 * a.tt);  // keys visible to the last row of B
   const int nkv = (kv_end + kBN - 1) / kBN;
 
   extern __shared__ uint8_t smem_raw[];
@@ -123,190 +171,177 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    mbar_init(&bar.q_full, 128);
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&bar.k_full[i], 1);
-      mbar_init(&bar.k_empty[i], 1);
-      mbar_init(&bar.v_full[i], 1);
-      mbar_init(&bar.v_empty[i], 1);
+    mbar_init(&bar.q_full, 1);
+    for (int i = 0; i < kKStages; ++i) { mbar_init(&bar.k_full[i], 1); mbar_init(&bar.k_empty[i], 1); }
+    for (int i = 0; i < kVStages; ++i) { mbar_init(&bar.v_full[i], 1); mbar_init(&bar.v_empty[i], 1); }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar.s_full[i], 1);
+      mbar_init(&bar.p_full[i], kBM);
+      mbar_init(&bar.o_final[i], 1);
     }
-    for (int i = 0; i < 2; ++i) mbar_init(&bar.s_full[i], 1);
-    mbar_init(&bar.p_full, 128);
-    mbar_init(&bar.o_done, 1);
-    bar.abort = 0;
     fence_mbar_init();
   }
-  if (warp == 5) tmem_alloc(&bar.tmem_base, 512);
+  if (warp == kWarpMma) tmem_alloc(&bar.tmem_base, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bar.tmem_base;
   bool ok = true;
 
-  if (warp == 4) {
-    // ------------------------------------------------------------ producer
-    // whole warp: lanes hold page coordinates, lane 0 issues the copies
-    const int32_t *row = a.bt + (size_t)s * a.bt_stride;
-    int cur = page_tok0(a, row, 0, lane);
-    int nxt = nkv > 4 ? page_tok0(a, row, 1, lane) : 0;
-    if (lane == 0) { tma_prefetch_desc(&tmk); tma_prefetch_desc(&tmv); }
-    for (int j = 0; j < nkv && ok; ++j) {
-      const int st = j % kStages, jj = j & 3;
-      const uint32_t use = j / kStages;  // how many times this stage was filled before
-      if (jj == 0 && j > 0) {
-        cur = nxt;
-        nxt = j + 4 < nkv ? page_tok0(a, row, (j >> 2) + 1, lane) : 0;
+  if (warp == kWarpK) {
+    // ------------------------------------------------------------ Q + K producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmq); tma_prefetch_desc(&tmk); tma_prefetch_desc(&tmv);
+      mbar_arrive_expect_tx(&bar.q_full, 2 * kTile);
+      for (int t = 0; t < 2; ++t) {
+        const int tok = q0 + tq0 + t * a.tt;
+        tma_load_3d(smem + OFF_Q + t * kTile, &tmq, &bar.q_full, 0, h * a.g, tok);
+        tma_load_3d(smem + OFF_Q + t * kTile + kHalf, &tmq, &bar.q_full, 64, h * a.g, tok);
       }
-      if (use > 0) ok = mbar_wait(&bar.k_empty[st], (use - 1) & 1);
-      if (!ok) break;
-      if (lane == 0) mbar_arrive_expect_tx(&bar.k_full[st], kTile);
-      load_kv_tile(&tmk, smem + OFF_K + st * kTile, &bar.k_full[st], a, h, cur, jj, lane);
-      if (use > 0) ok = mbar_wait(&bar.v_empty[st], (use - 1) & 1);
-      if (!ok) break;
-      if (lane == 0) mbar_arrive_expect_tx(&bar.v_full[st], kTile);
-      load_kv_tile(&tmv, smem + OFF_V + st * kTile, &bar.v_full[st], a, h, cur, jj, lane);
     }
-  } else if (warp == 5) {
+    ok = produce_kv<kKStages>(&tmk, smem + OFF_K, bar.k_full, bar.k_empty, a, s, h, nkv, lane);
+  } else if (warp == kWarpV) {
+    // ------------------------------------------------------------ V producer
+    ok = produce_kv<kVStages>(&tmv, smem + OFF_V, bar.v_full, bar.v_empty, a, s, h, nkv, lane);
+  } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_qk = umma_idesc_bf16(kBM, kBN, false);
       constexpr uint32_t idesc_pv = umma_idesc_bf16(kBM, kD, true);
-      const uint32_t sk = smem_u32(smem + OFF_K), sv = smem_u32(smem + OFF_V);
-      auto issue_qk = [&](int j) -> bool {
-        const int st = j % kStages;
-        if (!mbar_wait(&bar.k_full[st], (j / kStages) & 1)) return false;
-        tc_fence_after();
-        const uint32_t kb = sk + st * kTile;
+      const uint32_t sq = smem_u32(smem + OFF_Q), sk = smem_u32(smem + OFF_K),
+                     sv = smem_u32(smem + OFF_V);
+      // S_t = Q_t K_j^T (both operands from smem, K-major)
+      auto qk = [&](int t, int j) {
+        const uint32_t kb = sk + (j % kKStages) * kTile, qb = sq + t * kTile;
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
-          // A = Q (TMEM, 8 columns per 16 dims), B = K tile (K-major, swizzled)
-          umma_ts(tmem + TM_S + (j & 1) * kBN, tmem + TM_Q + kk * 8,
-                  umma_desc_sw128(kb + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024), idesc_qk,
-                  kk > 0 ? 1u : 0u);
+          const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
+          umma_ss(tmem + TM_S + t * kBM, umma_desc_sw128(qb + off, 16, 1024),
+                  umma_desc_sw128(kb + off, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&bar.s_full[j & 1]);
-        umma_commit(&bar.k_empty[st]);
-        return true;
+        umma_commit(&bar.s_full[t]);
       };
-      ok = mbar_wait(&bar.q_full, 0);
-      tc_fence_after();
-      if (ok) ok = issue_qk(0);
-      for (int j = 0; j < nkv && ok; ++j) {
-        // S_(j+1) overwrites the buffer of P_(j-1); PV_(j-1) was issued
-        // before it and tcgen05 MMAs of one thread execute in issue order.
-        if (j + 1 < nkv) {
-          ok = issue_qk(j + 1);
-          if (!ok) break;
-        }
-        const int st = j % kStages;
-        ok = mbar_wait(&bar.p_full, j & 1);
-        if (ok) ok = mbar_wait(&bar.v_full[st], (j / kStages) & 1);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t vb = sv + st * kTile;
+      // O_t += P_t V_j (P from TMEM over S_t, V MN-major in smem)
+      auto pv = [&](int t, int j) {
+        const uint32_t vb = sv + (j % kVStages) * kTile;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
-          // A = P (TMEM, aliased on S_(j&1)), B = V tile (MN-major: keys x dims)
-          umma_ts(tmem + TM_O, tmem + TM_S + (j & 1) * kBN + kk * 8,
+          umma_ts(tmem + TM_O + t * kBM, tmem + TM_S + t * kBM + kk * 8,
                   umma_desc_sw128(vb + kk * 2048, kHalf, 1024), idesc_pv,
                   (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&bar.o_done);
-        umma_commit(&bar.v_empty[st]);
+      };
+      ok = mbar_wait(&bar.q_full, 0) && mbar_wait(&bar.k_full[0], 0);
+      if (ok) {
+        tc_fence_after();
+        qk(0, 0);
+        qk(1, 0);
+        umma_commit(&bar.k_empty[0]);
+      }
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int vs = j % kVStages;
+        const bool more = j + 1 < nkv;
+        // tile A: PV_A(j), then S_A(j+1) (after PV_A(j) in issue order, which
+        // the tensor core preserves, so P_A(j) is consumed before it is overwritten)
+        ok = mbar_wait(&bar.p_full[0], j & 1) && mbar_wait(&bar.v_full[vs], (j / kVStages) & 1);
+        if (ok && more) ok = mbar_wait(&bar.k_full[(j + 1) % kKStages], ((j + 1) / kKStages) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        pv(0, j);
+        if (!more) umma_commit(&bar.o_final[0]);
+        if (more) qk(0, j + 1);
+        // tile B
+        ok = mbar_wait(&bar.p_full[1], j & 1);
+        if (!ok) break;
+        tc_fence_after();
+        pv(1, j);
+        umma_commit(&bar.v_empty[vs]);
+        if (!more) umma_commit(&bar.o_final[1]);
+        if (more) {
+          qk(1, j + 1);
+          umma_commit(&bar.k_empty[(j + 1) % kKStages]);
+        }
       }
     }
   } else {
     // ------------------------------------------------------------ softmax
-    const int r = threadIdx.x;  // row of the Q tile == TMEM lane
-    const int tq = tq0 + r / a.g;
+    const int t = warp >> 2;                  // Q tile (A = 0, B = 1)
+    const int r = threadIdx.x & (kBM - 1);    // row of the tile == TMEM lane
+    const int tq = tq0 + t * a.tt + r / a.g;  // token within the sequence
     const int qpos = p0 + tq;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    {
-      // this row of Q -> TMEM (two bf16 per column); rows past the tensor are 0
-      uint32_t qv[64];
-      const int64_t tok = (int64_t)q0 + tq;
-      if (tok < a.num_tokens) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(
-            a.q + (tok * a.Hq + (int64_t)h * a.g + (r % a.g)) * kD);
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const uint4 w = __ldg(src + c);
-          qv[4 * c] = w.x; qv[4 * c + 1] = w.y; qv[4 * c + 2] = w.z; qv[4 * c + 3] = w.w;
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) qv[c] = 0u;
-      }
-      tmem_st64_sync(tmem + lane_base + TM_Q, qv);
-      tc_fence_before();
-      mbar_arrive(&bar.q_full);
-    }
+    const int qpos_min = p0 + tq0 + t * a.tt;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_base + TM_S + t * kBM;
+    const uint32_t tO = tmem + lane_base + TM_O + t * kBM;
     float m_run = -INFINITY, l_run = 0.f;
     float sv[kBN];
     for (int j = 0; j < nkv; ++j) {
-      const int b = j & 1;
-      ok = mbar_wait(&bar.s_full[b], (j >> 1) & 1);
-      if (!ok) break;
+      ok = mbar_wait(&bar.s_full[t], j & 1);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      tmem_ld128(tmem + lane_base + TM_S + b * kBN, sv);
-
+      tmem_ld128(tS, sv);
       const int kbase = j * kBN;
-      const bool masked = kbase + kBN - 1 > qpos_min;
-      float mx = -INFINITY;
-      if (masked) {
+      if (kbase + kBN - 1 > qpos_min) {
 #pragma unroll
         for (int i = 0; i < kBN; ++i) {
           if (kbase + i > qpos) sv[i] = -INFINITY;
-          mx = fmaxf(mx, sv[i]);
         }
-      } else {
-#pragma unroll
-        for (int i = 0; i < kBN; ++i) mx = fmaxf(mx, sv[i]);
       }
+      // 8 independent max / sum chains
+      float mx8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx8[k] = sv[k];
+#pragma unroll
+      for (int i = 8; i < kBN; i += 8) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], sv[i + k]);
+      }
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       // scores are raw q.k; the softmax scale (and log2 e) folds into one FFMA
       const float m_new = fmaxf(m_run, mx * a.scale_log2);
       const bool need = j > 0 && (m_new - m_run > kRescaleThreshold);
       const float m_use = (j == 0 || need) ? m_new : m_run;
       const float corr = j == 0 ? 0.f : fast_exp2(m_run - m_use);
-      float sum = 0.f;
+      float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < kBN; ++i) {
-        sv[i] = fast_exp2(fmaf(sv[i], a.scale_log2, -m_use));
-        sum += sv[i];
-      }
-      l_run = l_run * corr + sum;
-      m_run = m_use;
-
-      if (j >= 1) {
-        ok = mbar_wait(&bar.o_done, (j - 1) & 1);
-        if (!ok) break;
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, need)) {
-#pragma unroll 1
-          for (int c = 0; c < kD / 32; ++c) {
-            float t[32];
-            const uint32_t ta = tmem + lane_base + TM_O + c * 32;
-            tmem_ld32(ta, t);
+      for (int i = 0; i < kBN; i += 8) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) t[i] *= corr;
-            tmem_st32(ta, t);
-          }
-          tmem_st_wait();
+        for (int k = 0; k < 8; ++k) {
+          const float x = fmaf(sv[i + k], a.scale_log2, -m_use);
+          sv[i + k] = ((kEmuMask >> k) & 1u) ? poly_exp2(x) : fast_exp2(x);
+          sum8[k] += sv[i + k];
         }
       }
-      // P row r (bf16 pairs) -> TMEM over the first 64 columns of S_b
-      {
-        uint32_t pv[64];
+      const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) +
+                        ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+      l_run = l_run * corr + sum;
+      m_run = m_use;
+      // PV_t(j-1) completed before S_t(j) (commit after QK_t(j) covers it),
+      // so O may be rescaled here without another wait.
+      if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+        for (int c = 0; c < kD / 32; ++c) {
+          float o[32];
+          tmem_ld32(tO + c * 32, o);
 #pragma unroll
-        for (int c = 0; c < 64; ++c) pv[c] = pack_bf16(sv[2 * c], sv[2 * c + 1]);
-        tmem_st64_sync(tmem + lane_base + TM_S + b * kBN, pv);
+          for (int i = 0; i < 32; ++i) o[i] *= corr;
+          tmem_st32(tO + c * 32, o);
+        }
+        tmem_st_wait();
+      }
+      {
+        uint32_t pw[64];
+#pragma unroll
+        for (int c = 0; c < 64; ++c) pw[c] = pack_bf16(sv[2 * c], sv[2 * c + 1]);
+        tmem_st64_sync(tS, pw);
       }
       tc_fence_before();
-      mbar_arrive(&bar.p_full);
+      mbar_arrive(&bar.p_full[t]);
     }
     // ---- epilogue: O / l -> bf16 rows of the packed output
-    if (ok) ok = mbar_wait(&bar.o_done, (nkv - 1) & 1);
-    if (ok) {
+    if (ok) ok = mbar_wait(&bar.o_final[t], 0);
+    if (__all_sync(0xffffffffu, ok)) {
       tc_fence_after();
       const float inv = 1.f / l_run;
       const bool valid = tq < n && q0 + tq < a.num_tokens;
@@ -314,27 +349,29 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
           a.out + ((size_t)(q0 + tq) * a.Hq + (size_t)h * a.g + (r % a.g)) * kD;
 #pragma unroll 1
       for (int c = 0; c < kD / 32; ++c) {
-        float t[32];
-        tmem_ld32(tmem + lane_base + TM_O + c * 32, t);
+        float o[32];
+        tmem_ld32(tO + c * 32, o);
         if (valid) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
             uint4 w;
-            w.x = pack_bf16(t[i] * inv, t[i + 1] * inv);
-            w.y = pack_bf16(t[i + 2] * inv, t[i + 3] * inv);
-            w.z = pack_bf16(t[i + 4] * inv, t[i + 5] * inv);
-            w.w = pack_bf16(t[i + 6] * inv, t[i + 7] * inv);
+            w.x = pack_bf16(o[i] * inv, o[i + 1] * inv);
+            w.y = pack_bf16(o[i + 2] * inv, o[i + 3] * inv);
+            w.z = pack_bf16(o[i + 4] * inv, o[i + 5] * inv);
+            w.w = pack_bf16(o[i + 6] * inv, o[i + 7] * inv);
             *reinterpret_cast<uint4 *>(orow + c * 32 + i) = w;
           }
         }
       }
+    } else {
+      ok = false;
     }
   }
   if (!ok) atomicExch(a.err, 1);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 5) tmem_dealloc(tmem, 512);
+  if (warp == kWarpMma) tmem_dealloc(tmem, 512);
 }
 
 // Rows of the packed output past cu_seqlens_q[num_seqs] (bucket padding) -> 0,
@@ -393,8 +430,11 @@ extern "C" vj_status vj_paged_prefill(
     return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_paged_prefill: null pointer");
   }
   const int tt = kBM / g;
-  CUtensorMap tmk, tmv;
-  int rc = VJ_OK;
+  CUtensorMap tmq, tmk, tmv;
+  // Q: dims (D, Hq, tokens); one box = the g heads of tt tokens, 64 dims
+  int rc = encode_tmap_3d(&tmq, q, kD, num_q_heads, num_tokens, (uint64_t)kD * 2,
+                          (uint64_t)num_q_heads * kD * 2, 64, g, tt, true);
+  if (rc) return rc;
   const uint64_t ntok = (uint64_t)num_blocks * block_size;
   const bool head_major = stride_head < stride_token;
   for (int i = 0; i < 2; ++i) {
@@ -407,7 +447,6 @@ extern "C" vj_status vj_paged_prefill(
     if (rc) return rc;
   }
   PrefillArgs a;
-  a.q = static_cast<const __nv_bfloat16 *>(q);
   a.out = static_cast<__nv_bfloat16 *>(out);
   a.bt = block_tables;
   a.cu = cu_seqlens_q;
@@ -424,15 +463,15 @@ extern "C" vj_status vj_paged_prefill(
   a.err = error_flag;
 
   const int64_t maxq = max_seqlen_q > 0 ? max_seqlen_q : num_tokens;
-  const int64_t mtiles = (maxq + tt - 1) / tt;
-  if (num_seqs > 0 && mtiles > 0) {
-    if (mtiles > INT32_MAX || num_kv_heads > 65535 || num_seqs > 65535) {
+  const int64_t mpairs = (maxq + 2 * tt - 1) / (2 * tt);
+  if (num_seqs > 0 && mpairs > 0) {
+    if (mpairs > INT32_MAX || num_kv_heads > 65535 || num_seqs > 65535) {
       return set_error(VJ_ERR_UNSUPPORTED, "vj_paged_prefill: grid too large");
     }
     cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)kSmemBytes);
-    dim3 grid((unsigned)mtiles, num_kv_heads, num_seqs);
-    prefill_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tmk, tmv, a);
+    dim3 grid((unsigned)mpairs, num_kv_heads, num_seqs);
+    prefill_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tmq, tmk, tmv, a);
     rc = check_launch("vj_paged_prefill");
     if (rc) return rc;
   }
