@@ -149,6 +149,7 @@ VJ_DEV bool produce_kv(const CUtensorMap *tm, uint8_t *ring, uint64_t *full, uin
   return true;
 }
 
+// 11 warps: a sub-partition holds 3 of them in its 16K registers -> <= 168 each.
 __global__ void __launch_bounds__(kThreads, 1)
 prefill_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                const __grid_constant__ CUtensorMap tmv, PrefillArgs a) {
@@ -303,15 +304,26 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
       const bool need = j > 0 && (m_new - m_run > kRescaleThreshold);
       const float m_use = (j == 0 || need) ? m_new : m_run;
       const float corr = j == 0 ? 0.f : fast_exp2(m_run - m_use);
+      // exponentials, row sum and P (bf16 pairs) in two 64-key halves so P
+      // of the first half is in TMEM before the second half is computed
       float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < kBN; i += 8) {
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t pw[32];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float x = fmaf(sv[i + k], a.scale_log2, -m_use);
-          sv[i + k] = ((kEmuMask >> k) & 1u) ? poly_exp2(x) : fast_exp2(x);
-          sum8[k] += sv[i + k];
+        for (int i = 0; i < kBN / 2; i += 8) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float x = fmaf(sv[hf * 64 + i + k], a.scale_log2, -m_use);
+            sv[hf * 64 + i + k] = ((kEmuMask >> k) & 1u) ? poly_exp2(x) : fast_exp2(x);
+            sum8[k] += sv[hf * 64 + i + k];
+          }
+#pragma unroll
+          for (int k = 0; k < 8; k += 2) {
+            pw[(i + k) / 2] = pack_bf16(sv[hf * 64 + i + k], sv[hf * 64 + i + k + 1]);
+          }
         }
+        tmem_st32u_nowait(tS + hf * 32, pw);
       }
       const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) +
                         ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
@@ -330,12 +342,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
         }
         tmem_st_wait();
       }
-      {
-        uint32_t pw[64];
-#pragma unroll
-        for (int c = 0; c < 64; ++c) pw[c] = pack_bf16(sv[2 * c], sv[2 * c + 1]);
-        tmem_st64_sync(tS, pw);
-      }
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&bar.p_full[t]);
     }
