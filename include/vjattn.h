@@ -123,6 +123,35 @@ VJ_API vj_status vj_paged_decode(
     cudaStream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * K2 for callers that cannot allocate device memory. No counterpart in the
+ * reference: it exists for callers such as a custom-call handler inside an
+ * XLA/JAX computation (the runtime owns all device memory, and a cudaMalloc
+ * there would bypass it and may synchronise the device) or a server that
+ * fixes its memory budget at start-up.
+ *
+ * Same inputs, outputs and semantics as vj_paged_decode, without the
+ * workspace: the split-KV scratch lives in a fixed 16 MiB device array
+ * (vj_paged_decode_noalloc_scratch_bytes()) that every GPU loading this
+ * library keeps until the process exits. Shapes whose scratch does not fit
+ * (batch must stay below ~16 MiB / (Hq * 520 B), e.g. < 1008 sequences at
+ * Hq = 32) return VJ_ERR_UNSUPPORTED. The first call on each device looks
+ * up the array's device address (cudaGetSymbolAddress); make that first call
+ * before any stream capture. All calls on a device share the array and it
+ * keeps the last call's contents (every word a call reads is rewritten by
+ * that call first); calls whose kernels overlap on the GPU race on it, so
+ * order them on one stream. It allocates nothing.
+ * ------------------------------------------------------------------------- */
+VJ_API size_t vj_paged_decode_noalloc_scratch_bytes(void);
+
+VJ_API vj_status vj_paged_decode_noalloc(
+    const void *q, const void *k_cache, const void *v_cache,
+    const int32_t *block_tables, const int32_t *context_lens, void *out,
+    int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+    int64_t num_blocks, int32_t block_size, int32_t bt_width, int32_t bt_stride,
+    int64_t stride_block, int64_t stride_token, int64_t stride_head,
+    float scale, cudaStream_t stream);
+
+/* ---------------------------------------------------------------------------
  * K1: varlen paged prefill attention (causal), tcgen05/TMEM tiles fed by TMA.
  * Replaces vllm/kernels/prefill_paged_attention.py:407-453
  * (prefill_paged_attention) incl. the Q gather (:227-239), split merge

@@ -21,6 +21,7 @@
 #include "../../include/vjattn.h"
 #include "vj_common.cuh"
 
+#include <mutex>
 #include <string>
 
 namespace vj {
@@ -497,4 +498,100 @@ extern "C" vj_status vj_paged_decode(
   const int warps = batch * num_q_heads;
   decode_combine_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(a);
   return check_launch("vj_paged_decode(combine)");
+}
+
+// ---------------------------------------------------------------------------
+// Decode for callers that cannot allocate device memory.
+//
+// Some callers may not call cudaMalloc at all: a custom-call handler inside
+// an XLA / JAX computation, where the runtime owns every device buffer and an
+// allocation inside the handler would bypass its accounting and may
+// synchronise the device, or a serving process that pins its whole memory
+// budget at start-up. vj_paged_decode_noalloc takes the same inputs and
+// outputs as vj_paged_decode but keeps its split-KV scratch in a fixed
+// file-scope device array instead of a caller workspace.
+//
+// The array (kStaticScratchBytes) exists on every GPU that loads this
+// library and stays allocated until the process exits. All calls on a device
+// share it and it keeps the previous call's contents; the plan kernel
+// rewrites every word a call reads before it is read, so nothing needs
+// clearing, but two calls whose kernels overlap on the GPU (different
+// streams, no ordering between them) race on the array.
+// ---------------------------------------------------------------------------
+namespace vj {
+namespace {
+constexpr size_t kStaticScratchBytes = size_t(16) << 20;  // 16 MiB per device
+__device__ __align__(256) uint8_t g_decode_scratch[kStaticScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void *g_scratch_dev_ptr[kMaxDevices] = {nullptr};
+
+// Device address of g_decode_scratch on the current device. In host code the
+// symbol only names a host-side stand-in, so the address is looked up once
+// per device (with that device current) and cached.
+int scratch_address(void **ptr) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    return set_error(VJ_ERR_CUDA, std::string("vj_paged_decode_noalloc: cudaGetDevice: ") +
+                                      cudaGetErrorString(e));
+  }
+  if (dev < 0 || dev >= kMaxDevices) {
+    return set_error(VJ_ERR_UNSUPPORTED, "vj_paged_decode_noalloc: device index out of range");
+  }
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_dev_ptr[dev] == nullptr) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      return set_error(VJ_ERR_CUDA, std::string("vj_paged_decode_noalloc: cudaGetSymbolAddress: ") +
+                                        cudaGetErrorString(e));
+    }
+    g_scratch_dev_ptr[dev] = p;
+  }
+  *ptr = g_scratch_dev_ptr[dev];
+  return VJ_OK;
+}
+}  // namespace
+}  // namespace vj
+
+extern "C" size_t vj_paged_decode_noalloc_scratch_bytes(void) { return vj::kStaticScratchBytes; }
+
+extern "C" vj_status vj_paged_decode_noalloc(
+    const void *q, const void *k_cache, const void *v_cache, const int32_t *block_tables,
+    const int32_t *context_lens, void *out, int32_t batch, int32_t num_q_heads,
+    int32_t num_kv_heads, int32_t head_dim, int64_t num_blocks, int32_t block_size,
+    int32_t bt_width, int32_t bt_stride, int64_t stride_block, int64_t stride_token,
+    int64_t stride_head, float scale, cudaStream_t stream) {
+  using namespace vj;
+  if (batch < 0 || num_q_heads <= 0 || head_dim != kD) {
+    // let the shared entry point produce its usual argument message
+    return vj_paged_decode(q, k_cache, v_cache, block_tables, context_lens, out, batch,
+                           num_q_heads, num_kv_heads, head_dim, num_blocks, block_size, bt_width,
+                           bt_stride, stride_block, stride_token, stride_head, scale, 0, nullptr,
+                           0, stream);
+  }
+  // Largest split budget whose scratch fits the fixed array.
+  const size_t per_chunk = (size_t)num_q_heads * (sizeof(float2) + sizeof(float) * kD);
+  int64_t max_chunks = (int64_t)(kStaticScratchBytes / per_chunk);
+  while (max_chunks > 0 &&
+         vj::workspace_bytes(batch, num_q_heads, (int)max_chunks) > kStaticScratchBytes) {
+    --max_chunks;
+  }
+  if (max_chunks <= batch) {
+    return set_error(VJ_ERR_UNSUPPORTED,
+                     "vj_paged_decode_noalloc: batch " + std::to_string(batch) + " with " +
+                         std::to_string(num_q_heads) + " query heads needs more than the " +
+                         std::to_string(kStaticScratchBytes >> 20) +
+                         " MiB fixed scratch (at most " + std::to_string(max_chunks - 1) +
+                         " sequences at this head count); use vj_paged_decode with a workspace");
+  }
+  void *scratch = nullptr;
+  int rc = scratch_address(&scratch);
+  if (rc) return rc;
+  return vj_paged_decode(q, k_cache, v_cache, block_tables, context_lens, out, batch,
+                         num_q_heads, num_kv_heads, head_dim, num_blocks, block_size, bt_width,
+                         bt_stride, stride_block, stride_token, stride_head, scale,
+                         (int32_t)max_chunks, scratch, kStaticScratchBytes, stream);
 }

@@ -34,6 +34,13 @@ PROTOTYPES: dict[str, tuple] = {
         c_i32, c_i32,                               # bt_width, bt_stride
         c_i64, c_i64, c_i64,                        # strides
         c_f32, c_i32, c_vp, c_sz, c_vp]),           # scale, max_chunks, ws, ws_bytes, stream
+    "vj_paged_decode_noalloc_scratch_bytes": (c_sz, []),
+    "vj_paged_decode_noalloc": (c_int, [
+        c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,         # q, k_cache, v_cache, bt, lens, out
+        c_i32, c_i32, c_i32, c_i32, c_i64, c_i32,   # B, Hq, Hkv, D, nb, bs
+        c_i32, c_i32,                               # bt_width, bt_stride
+        c_i64, c_i64, c_i64,                        # strides
+        c_f32, c_vp]),                              # scale, stream
     "vj_paged_prefill": (c_int, [
         c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,   # q, k, v, bt, cu_q, ctx_lens, out
         c_i64, c_i32, c_i32, c_i32, c_i32,          # T, S, Hq, Hkv, D
