@@ -180,6 +180,61 @@ VJ_API vj_status vj_paged_prefill(
     int64_t stride_head, int32_t max_seqlen_q, float scale,
     int32_t *error_flag, cudaStream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * K4: batch metadata built on the GPU from device-resident engine state.
+ * Replaces vllm/src/model_runner.py:204-214 (pad_block_tables), :217-266
+ * (prepare_prefill) and :268-301 (prepare_decode); the outputs equal the
+ * reference's arrays element for element.
+ *
+ * Engine state, indexed by request slot (device, int32):
+ *   token_table [max_slots, token_stride]  token ids of each request
+ *   block_pool  [max_slots, bt_stride]     its allocated block ids
+ *   num_blocks  [max_slots]                number of valid entries
+ * Per call: seq_slots[num_seqs], seq_lens[num_seqs] (= len(request)).
+ * Prefill (mode VJ_META_PREFILL): all len tokens of each sequence, packed;
+ *   input_ids/positions/slot_mapping [bucket_tokens] padded with 0/0/-1;
+ *   cu_seqlens [bucket_batch + 1] padded by repeating the total;
+ *   block_tables [bucket_batch, width] padded with -1.
+ * Decode (VJ_META_DECODE): one row per sequence (last token, position
+ *   len-1, context_lens = len), rows [num_seqs, bucket_tokens) padded with
+ *   0/0/0/-1; block_tables [bucket_batch = bucket_tokens, width].
+ *   flags & VJ_META_LAST_BLOCK_SLOT: slot = last allocated block * bs +
+ *   (len-1) % bs, exactly as model_runner.py:282-284 (differs from the
+ *   block holding position len-1 right after a block-boundary allocation).
+ * error_flag (device int32) is set to 1 (position without an allocated
+ * block), 2 (tokens exceed bucket_tokens) or 3 (bad scatter row).
+ * ------------------------------------------------------------------------- */
+enum { VJ_META_PREFILL = 0, VJ_META_DECODE = 1 };
+enum { VJ_META_LAST_BLOCK_SLOT = 1 };
+
+VJ_API vj_status vj_build_metadata(
+    int32_t mode, const int32_t *seq_slots, const int32_t *seq_lens,
+    int32_t num_seqs, const int32_t *token_table, int32_t token_stride,
+    const int32_t *block_pool, const int32_t *num_blocks, int32_t bt_stride,
+    int32_t block_size, int32_t width, int32_t bucket_tokens,
+    int32_t bucket_batch, int32_t flags, int32_t *input_ids, int32_t *positions,
+    int32_t *slot_mapping, int32_t *block_tables, int32_t *cu_seqlens,
+    int32_t *context_lens, int32_t *error_flag, cudaStream_t stream);
+
+/* Host-delta upload into a device table (block_pool or token_table):
+ * headers [num_rows, 4] = (row, start, count, payload offset); writes
+ * table[row][start, start+count) from payload and, if row_len is not NULL,
+ * row_len[row] = start + count. A row may appear at most once per call. */
+VJ_API vj_status vj_scatter_rows(const int32_t *headers, const int32_t *payload,
+                                 int32_t num_rows, int32_t *table,
+                                 int32_t table_stride, int32_t max_cols,
+                                 int32_t *row_len, int32_t *error_flag,
+                                 cudaStream_t stream);
+
+/* Greedy sampling, vllm/sampler.py:13-15 (argmax over bf16 logits, first
+ * index on ties): out_tokens[r] = argmax(logits[r, :vocab]); if token_table
+ * is given the token is also stored at token_table[seq_slots[r]][seq_lens[r]]. */
+VJ_API vj_status vj_argmax_append(const void *logits, int64_t row_stride,
+                                  int32_t num_rows, int32_t vocab,
+                                  int32_t *out_tokens, int32_t *token_table,
+                                  int32_t token_stride, const int32_t *seq_slots,
+                                  const int32_t *seq_lens, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -47,11 +47,22 @@ PROTOTYPES: dict[str, tuple] = {
         c_i64, c_i32, c_i32, c_i32,                 # nb, bs, bt_width, bt_stride
         c_i64, c_i64, c_i64,                        # strides
         c_i32, c_f32, c_vp, c_vp]),                 # max_seqlen_q, scale, err, stream
+    "vj_build_metadata": (c_int, [
+        c_i32, c_vp, c_vp, c_i32,                   # mode, seq_slots, seq_lens, num_seqs
+        c_vp, c_i32, c_vp, c_vp, c_i32,             # token_table, stride, block_pool, nblocks, bt_stride
+        c_i32, c_i32, c_i32, c_i32, c_i32,          # block_size, width, bucket_tokens, bucket_batch, flags
+        c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,         # ids, positions, slots, block_tables, cu, ctx
+        c_vp, c_vp]),                               # error_flag, stream
+    "vj_scatter_rows": (c_int, [c_vp, c_vp, c_i32, c_vp, c_i32, c_i32, c_vp, c_vp, c_vp]),
+    "vj_argmax_append": (c_int, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_i32, c_vp, c_vp,
+                                 c_vp]),
 }
 
 # vj_status codes (include/vjattn.h)
 VJ_OK, VJ_ERR_INVALID_ARGUMENT, VJ_ERR_UNSUPPORTED, VJ_ERR_WORKSPACE, VJ_ERR_CUDA = range(5)
 VJ_KV_NORM, VJ_KV_ROPE, VJ_KV_WRAP_NEGATIVE = 1, 2, 4
+VJ_META_PREFILL, VJ_META_DECODE = 0, 1
+VJ_META_LAST_BLOCK_SLOT = 1
 
 
 class VJError(RuntimeError):

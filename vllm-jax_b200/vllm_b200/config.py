@@ -1,0 +1,29 @@
+"""Engine configuration (vllm/config.py:3-10 of vllm-jax, plus TP and memory knobs)."""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+
+@dataclass
+class Config:
+    model: str
+    max_num_batched_tokens: int
+    max_num_seqs: int
+    num_blocks: int
+    block_size: int
+    # additions of this build
+    tensor_parallel_size: int = 1
+    gpu_memory_utilization: float = 0.9   # used when num_blocks <= 0
+    max_model_len: int | None = None       # default: max_num_batched_tokens (reference)
+    # compat=True reproduces the reference's host-side behaviour bit for bit:
+    # finished requests keep their blocks (scheduler.py:65-70) and a decode
+    # token is stored in the last allocated block (model_runner.py:282-284).
+    compat: bool = True
+
+    @property
+    def max_len(self) -> int:
+        return self.max_model_len or self.max_num_batched_tokens
+
+    @property
+    def max_blocks_per_seq(self) -> int:
+        return (self.max_len + self.block_size - 1) // self.block_size

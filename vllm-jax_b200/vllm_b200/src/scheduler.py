@@ -1,0 +1,86 @@
+"""Continuous-batching scheduler (vllm/src/scheduler.py:7-70 of vllm-jax).
+
+Policy, identical to the reference:
+  * decode first: every running request (front first) gets one token while
+    fewer than max_num_seqs are scheduled and the token budget is not spent;
+    a request that needs a new block when none is free preempts the request
+    at the TAIL of `running` (it returns to the front of `waiting` and gives
+    its blocks back), and an empty `running` with no room raises the same
+    AssertionError as the reference;
+  * then prefill from the front of `waiting` while the sequence budget lasts,
+    the request fits strictly inside the remaining token budget
+    (num_batched + len < max_num_batched_tokens) and its blocks are free;
+  * postprocess finishes a request on EOS (unless ignore_eos) or when it has
+    max_new_tokens completions.
+With Config.compat = False finished requests also release their blocks (the
+reference keeps them, so its pool shrinks over a long run)."""
+from __future__ import annotations
+
+from collections import deque
+
+from ..config import Config
+from .kv_cache_manager import KVCacheManager
+from .request import Request, Status
+
+
+class Scheduler:
+
+    def __init__(self, config: Config, kv_cache_manager: KVCacheManager):
+        self.max_num_batched_tokens = config.max_num_batched_tokens
+        self.max_num_seqs = config.max_num_seqs
+        self.compat = config.compat
+        self.kv_cache_manager = kv_cache_manager
+        self.waiting: deque[Request] = deque()
+        self.running: deque[Request] = deque()
+        self.finished_requests: list[Request] = []
+
+    def is_finished(self) -> bool:
+        return not self.waiting and not self.running
+
+    def add(self, request: Request) -> None:
+        self.waiting.append(request)
+
+    def preempt(self, request: Request) -> None:
+        request.status = Status.WAITING
+        self.waiting.appendleft(request)
+        self.kv_cache_manager.deallocate(request)
+
+    def schedule(self) -> tuple[list[Request], list[Request]]:
+        kv = self.kv_cache_manager
+        decode: list[Request] = []
+        prefill: list[Request] = []
+        num_tokens = num_seqs = 0
+        while (self.running and num_seqs < self.max_num_seqs
+               and num_tokens < self.max_num_batched_tokens):
+            request = self.running.popleft()
+            while not kv.can_allocate(request, False):
+                assert self.running, "Request cant fit in memory"
+                self.preempt(self.running.pop())
+            kv.allocate_slots(request, False)
+            decode.append(request)
+            num_seqs += 1
+            num_tokens += 1
+        self.running.extendleft(reversed(decode))
+        while self.waiting and num_seqs < self.max_num_seqs:
+            request = self.waiting[0]
+            if (num_tokens + len(request) >= self.max_num_batched_tokens
+                    or not kv.can_allocate(request, True)):
+                break
+            self.waiting.popleft()
+            self.running.append(request)
+            request.status = Status.RUNNING
+            kv.allocate_slots(request, True)
+            prefill.append(request)
+            num_seqs += 1
+            num_tokens += len(request)
+        return decode, prefill
+
+    def postprocess(self, requests: list[Request], token_ids: list[int]) -> None:
+        for request, token_id in zip(requests, token_ids):
+            if ((not request.ignore_eos and token_id == request.eos_token_id)
+                    or request.num_completion_tokens == request.max_new_tokens):
+                request.status = Status.FINISHED
+                self.running.remove(request)
+                self.finished_requests.append(request)
+                if not self.compat:
+                    self.kv_cache_manager.deallocate(request)
