@@ -76,7 +76,9 @@ VJ_API int vj_version(void);
  * Replaces vllm/model/qwen3.py:105-111 (_update_kv_cache, mode="drop") and
  * the q_norm/k_norm/apply_rope chain at qwen3.py:286-296 (apply_rope :59-78).
  *
- *   q_in [T,Hq,D], k_in [T,Hkv,D], v_in [T,Hkv,D]  bf16, token rows contiguous
+ *   q_in [T,Hq,D], k_in [T,Hkv,D], v_in [T,Hkv,D] bf16; token t of each
+ *   starts at base + t * *_row_stride elements (0 -> packed rows), so they
+ *   may be column slices of one fused qkv projection output
  *   q_norm_w, k_norm_w [D] bf16 (required with VJ_KV_NORM)
  *   positions [T] int32, slot_mapping [T] int32 (flat slot = block*bs + offset)
  *   q_out [T,Hq,D] bf16 (may equal q_in), k_out [T,Hkv,D] bf16 or NULL
@@ -94,6 +96,7 @@ VJ_API vj_status vj_kv_store_qknorm_rope(
     int64_t num_tokens, int32_t num_q_heads, int32_t num_kv_heads,
     int32_t head_dim, int64_t num_blocks, int32_t block_size,
     int64_t stride_block, int64_t stride_token, int64_t stride_head,
+    int64_t q_row_stride, int64_t k_row_stride, int64_t v_row_stride,
     float eps, float rope_theta, int32_t flags, cudaStream_t stream);
 
 /* ---------------------------------------------------------------------------

@@ -38,7 +38,8 @@ def test_validation_without_gpu():
     assert lib.vj_version() >> 16 == 1
     # head_dim 64 is rejected before any CUDA call
     st = lib.vj_kv_store_qknorm_rope(None, 1, 1, None, None, None, 1, None, None, 16, 16,
-                                     4, 0, 2, 64, 4, 16, 4096, 256, 128, 1e-6, 1e6, 0, None)
+                                     4, 0, 2, 64, 4, 16, 4096, 256, 128, 0, 0, 0, 1e-6, 1e6, 0,
+                                     None)
     assert st == _native.VJ_ERR_UNSUPPORTED
     assert b"head_dim" in lib.vj_get_last_error()
     st = lib.vj_paged_decode(1, 1, 1, 1, 1, 1, 2, 12, 8, 128, 10, 16, 4, 4, 16 * 1024, 1024,

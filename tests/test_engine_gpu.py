@@ -1,0 +1,156 @@
+"""End-to-end engine on the GPU: C1 greedy decoding vs the oracle, the
+reference-signature attention boundary, preemption and tensor-parallel setup."""
+import json
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as oatt
+from oracle.bf16 import bf16
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "host_traces.json")
+
+
+def _c1():
+    with open(GOLDEN) as f:
+        return next(s for s in json.load(f) if s["name"] == "c1")
+
+
+@pytest.fixture(scope="module")
+def c1_run():
+    """Qwen3-0.6B, random weights (seed 0, drawn on the CPU), the C1 prompts."""
+    from vllm_b200 import Config, SamplingParams
+    from vllm_b200.model.qwen3 import PRESETS, Qwen3Weights
+    from vllm_b200.src.engine import Engine
+    from vllm_b200.src.request import Request
+    sc = _c1()
+    cfg = PRESETS["Qwen3-0.6B"]
+    dev = torch.device("cuda", 0)
+    weights = Qwen3Weights(cfg, dev, seed=0, gen_device="cpu")
+    Request.reset_ids()
+    eng = Engine(Config(model="Qwen3-0.6B", **sc["config"]), dev, model_config=cfg,
+                 weights=weights, max_slots=16)
+    outs = eng.generate(sc["prompts"], SamplingParams(temperature=0.0, max_new_tokens=32,
+                                                      ignore_eos=True))
+    return sc, cfg, weights, eng, outs
+
+
+def test_c1_engine_runs_and_schedules_like_reference(c1_run):
+    sc, cfg, weights, eng, outs = c1_run
+    assert [len(o) for o in outs] == [32] * 4
+    assert eng.stats["steps"] == len(sc["steps"])           # same step count as the reference
+    # block ids the engine used are the reference's (same FIFO pool)
+    assert [b.block_id for b in eng.kv.free_block_queue] == sc["steps"][-1]["free_blocks"]
+
+
+def test_c1_greedy_tokens_vs_oracle(c1_run):
+    """Greedy tokens of the first 32 steps against the oracle's restatement of
+    the reference forward. Logits are bf16, so a top-2 gap of a few ulps can
+    flip argmax under any change of accumulation order; a divergence is only
+    accepted at such a near-tie, and the run must agree step for step until it."""
+    from oracle.qwen3 import OracleQwen3, greedy_replay
+    sc, cfg, weights, eng, outs = c1_run
+    model = OracleQwen3(cfg, weights.full_numpy(), sc["config"]["num_blocks"],
+                        sc["config"]["block_size"])
+    tokens, gaps = greedy_replay(model, sc, sc["prompts"])
+    n_match, first_div = 0, None
+    for r in range(4):
+        ref = tokens[r][len(sc["prompts"][r]):]
+        got = outs[r]
+        for step, (a, b) in enumerate(zip(got, ref)):
+            if a != b:
+                if first_div is None or step < first_div[1]:
+                    first_div = (r, step)
+                break
+            n_match += 1
+    print(f"greedy agreement: {n_match}/128 tokens before the first divergence per request; "
+          f"first divergence {first_div}")
+    if first_div is not None:
+        r, step = first_div
+        top, gap = gaps[step][r]
+        ulp = 2.0 ** (math.floor(math.log2(abs(max(1e-3, top)))) - 7) if top else 2 ** -7
+        lg = max(abs(x[0]) for x in gaps[step])
+        assert gap <= 4 * 2.0 ** (math.floor(math.log2(max(lg, 1.0))) - 7) + 1e-6, (
+            f"request {r} diverged at step {step} with an oracle top-2 gap of {gap}")
+    assert n_match >= 64
+
+
+def test_attention_boundary_reference_signature():
+    """attention(kv_cache, q, k, v, metadata) of vllm/model/qwen3.py:172-218."""
+    from vllm_b200.model.qwen3 import (DecodeAttentionMetadata, PrefillAttentionMetadata,
+                                       attention)
+    rng = np.random.default_rng(4)
+    nb, bs, Hkv, Hq, D = 32, 16, 8, 32, 128
+    t = lambda x, dt=torch.bfloat16: torch.from_numpy(np.ascontiguousarray(x)).to(dt).cuda()
+    cache = np.zeros((2, nb, bs, Hkv, D), np.float32)
+    # prefill of two sequences (20 and 37 tokens), padded to 64
+    lens = [20, 37]
+    blocks = [[3, 9], [0, 7, 12]]
+    slots, pos = [], []
+    for L, blk in zip(lens, blocks):
+        slots += [blk[i // bs] * bs + i % bs for i in range(L)]
+        pos += list(range(L))
+    T = 64
+    slots += [-1] * (T - len(slots))
+    pos += [0] * (T - len(pos))
+    q = bf16(rng.standard_normal((T, Hq, D)))
+    k = bf16(rng.standard_normal((T, Hkv, D)))
+    v = bf16(rng.standard_normal((T, Hkv, D)))
+    bt = np.full((4, 8), -1, np.int32)
+    for i, blk in enumerate(blocks):
+        bt[i, :len(blk)] = blk
+    cu = np.array([0, 20, 57, 57, 57], np.int32)
+    kc, vc = cache[0].copy(), cache[1].copy()
+    from oracle import kv_store as okv
+    okv.update_kv_cache(kc, vc, np.asarray(slots), k, v)
+    ref = oatt.prefill_attention(q, kc, vc, bt, cu[:3], np.array(lens), 1 / math.sqrt(D))
+    d_cache = t(cache)
+    meta = PrefillAttentionMetadata(t(pos, torch.int32), t(slots, torch.int32),
+                                    t(bt, torch.int32), t(cu, torch.int32), t(cu, torch.int32),
+                                    37, 37, 64, num_seqs=2)
+    d_cache, out = attention(d_cache, t(q), t(k), t(v), meta)
+    torch.cuda.synchronize()
+    err = np.abs(out.float().cpu().numpy() - ref)
+    assert err.max() <= 2e-2 and err.mean() <= 2e-3
+    np.testing.assert_array_equal(d_cache.float().cpu().numpy()[0], kc)
+    # decode of the same two sequences, one new token each
+    qd = bf16(rng.standard_normal((2, Hq, D)))
+    kd = bf16(rng.standard_normal((2, Hkv, D)))
+    vd = bf16(rng.standard_normal((2, Hkv, D)))
+    dslots = np.array([3 * bs + 4 if False else blocks[0][20 // bs] * bs + 20 % bs,
+                       blocks[1][37 // bs] * bs + 37 % bs], np.int32)
+    okv.update_kv_cache(kc, vc, dslots, kd, vd)
+    ctx = np.array([21, 38], np.int32)
+    ref = oatt.decode_attention(qd, kc, vc, bt[:2], ctx, 1 / math.sqrt(D))
+    dmeta = DecodeAttentionMetadata(t([20, 37], torch.int32), t(dslots, torch.int32),
+                                    t(bt[:2], torch.int32), t(ctx, torch.int32))
+    d_cache, out = attention(d_cache, t(qd), t(kd), t(vd), dmeta)
+    torch.cuda.synchronize()
+    err = np.abs(out.float().cpu().numpy() - ref)
+    assert err.max() <= 2e-2 and err.mean() <= 2e-3
+
+
+def test_engine_preemption_completes_without_compat():
+    """A pool too small for all requests forces tail preemption and re-prefill;
+    with compat=False (finished requests free their blocks) the run completes."""
+    from vllm_b200 import Config, SamplingParams
+    from vllm_b200.model.qwen3 import Qwen3Config, Qwen3Weights
+    from vllm_b200.src.engine import Engine
+    cfg = Qwen3Config(hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                      num_attention_heads=16, vocab_size=1000, tie_word_embeddings=True)
+    dev = torch.device("cuda", 0)
+    w = Qwen3Weights(cfg, dev, seed=1)
+    eng = Engine(Config(model="tiny", max_num_batched_tokens=256, max_num_seqs=3,
+                        num_blocks=11, block_size=16, compat=False), dev, model_config=cfg,
+                 weights=w, max_slots=16)
+    rng = np.random.default_rng(2)
+    prompts = [rng.integers(0, 1000, n).tolist() for n in (46, 17, 20, 28, 19, 58)]
+    outs = eng.generate(prompts, SamplingParams(temperature=0, max_new_tokens=27,
+                                                ignore_eos=True))
+    assert [len(o) for o in outs] == [27] * 6
+    assert eng.stats["prefill_tokens"] > sum(len(p) for p in prompts)   # re-prefills happened

@@ -62,6 +62,7 @@ kv_store_qknorm_rope_kernel(const __nv_bfloat16 *__restrict__ q_in,
                             __nv_bfloat16 *k_cache, __nv_bfloat16 *v_cache,
                             int64_t T, int Hq, int Hkv, int64_t num_slots,
                             int block_size, int64_t sb, int64_t st, int64_t sh,
+                            int64_t qrs, int64_t krs, int64_t vrs,
                             float eps, int flags, RopeTable rope) {
   __shared__ float2 cs[kTokPerCta][kPairs];
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kTokPerCta;
@@ -102,11 +103,11 @@ kv_store_qknorm_rope_kernel(const __nv_bfloat16 *__restrict__ q_in,
     int kind;  // 0 = q, 1 = k, 2 = v
     int h;
     if (hidx < Hq) {
-      kind = 0; h = hidx; src = q_in + (t * Hq + h) * kHeadDim; w = q_w;
+      kind = 0; h = hidx; src = q_in + t * qrs + h * kHeadDim; w = q_w;
     } else if (hidx < Hq + Hkv) {
-      kind = 1; h = hidx - Hq; src = k_in + (t * Hkv + h) * kHeadDim; w = k_w;
+      kind = 1; h = hidx - Hq; src = k_in + t * krs + h * kHeadDim; w = k_w;
     } else {
-      kind = 2; h = hidx - Hq - Hkv; src = v_in + (t * Hkv + h) * kHeadDim;
+      kind = 2; h = hidx - Hq - Hkv; src = v_in + t * vrs + h * kHeadDim;
     }
     uint4 raw = *reinterpret_cast<const uint4 *>(src + l16 * 8);
     uint32_t wd[4] = {raw.x, raw.y, raw.z, raw.w};
@@ -191,8 +192,8 @@ extern "C" vj_status vj_kv_store_qknorm_rope(
     void *q_out, void *k_out, void *k_cache, void *v_cache, int64_t num_tokens,
     int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
     int64_t num_blocks, int32_t block_size, int64_t stride_block,
-    int64_t stride_token, int64_t stride_head, float eps, float rope_theta,
-    int32_t flags, cudaStream_t stream) {
+    int64_t stride_token, int64_t stride_head, int64_t q_row_stride, int64_t k_row_stride,
+    int64_t v_row_stride, float eps, float rope_theta, int32_t flags, cudaStream_t stream) {
   using namespace vj;
   if (num_tokens < 0 || num_q_heads < 0 || num_kv_heads <= 0 || num_blocks <= 0 ||
       block_size <= 0) {
@@ -213,6 +214,15 @@ extern "C" vj_status vj_kv_store_qknorm_rope(
   if ((flags & VJ_KV_ROPE) && !positions) {
     return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_kv_store_qknorm_rope: VJ_KV_ROPE needs positions");
   }
+  if (q_row_stride == 0) q_row_stride = (int64_t)num_q_heads * kHeadDim;
+  if (k_row_stride == 0) k_row_stride = (int64_t)num_kv_heads * kHeadDim;
+  if (v_row_stride == 0) v_row_stride = (int64_t)num_kv_heads * kHeadDim;
+  if ((q_row_stride | k_row_stride | v_row_stride) % 8 != 0 ||
+      (reinterpret_cast<uintptr_t>(q_in) | reinterpret_cast<uintptr_t>(k_in) |
+       reinterpret_cast<uintptr_t>(v_in)) % 16 != 0) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT,
+                     "vj_kv_store_qknorm_rope: q/k/v rows must start on 16-byte boundaries");
+  }
   if ((stride_block | stride_token | stride_head) % 8 != 0 ||
       (reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) % 16 != 0) {
     return set_error(VJ_ERR_INVALID_ARGUMENT,
@@ -228,6 +238,6 @@ extern "C" vj_status vj_kv_store_qknorm_rope(
       static_cast<__nv_bfloat16 *>(q_out), static_cast<__nv_bfloat16 *>(k_out),
       static_cast<__nv_bfloat16 *>(k_cache), static_cast<__nv_bfloat16 *>(v_cache), num_tokens,
       num_q_heads, num_kv_heads, num_blocks * block_size, block_size, stride_block, stride_token,
-      stride_head, eps, flags, rope);
+      stride_head, q_row_stride, k_row_stride, v_row_stride, eps, flags, rope);
   return check_launch("vj_kv_store_qknorm_rope");
 }

@@ -26,6 +26,7 @@ PROTOTYPES: dict[str, tuple] = {
         c_vp, c_vp, c_vp, c_vp,                     # q_out, k_out, k_cache, v_cache
         c_i64, c_i32, c_i32, c_i32, c_i64, c_i32,   # T, Hq, Hkv, D, nb, bs
         c_i64, c_i64, c_i64,                        # strides (block, token, head)
+        c_i64, c_i64, c_i64,                        # q/k/v row strides (0 = packed)
         c_f32, c_f32, c_i32, c_vp]),                # eps, theta, flags, stream
     "vj_paged_decode_workspace_size": (c_sz, [c_i32, c_i32, c_i32, c_i32]),
     "vj_paged_decode": (c_int, [

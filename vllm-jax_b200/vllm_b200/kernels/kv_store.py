@@ -48,19 +48,20 @@ def kv_store_qknorm_rope(q: torch.Tensor | None, k: torch.Tensor, v: torch.Tenso
         raise ValueError(f"k and v must have the same shape. Got {tuple(k.shape)} and {tuple(v.shape)}")
     for name, t in (("k", k), ("v", v)):
         require_dtype(t, torch.bfloat16, name)
-        if not t.is_contiguous():
-            raise ValueError(f"`{name}` must be contiguous")
+        if t.stride(2) != 1 or t.stride(1) != D:
+            raise ValueError(f"`{name}` must have contiguous head rows ([T, H, D] with packed heads)")
     require_dtype(slot_mapping, torch.int32, "slot_mapping")
     if slot_mapping.shape != (T,):
         raise ValueError("slot_mapping must have shape [num_tokens]")
     Hq = 0
     if q is not None:
         require_dtype(q, torch.bfloat16, "q")
-        if q.dim() != 3 or q.shape[0] != T or q.shape[2] != D or not q.is_contiguous():
-            raise ValueError("q must be a contiguous [num_tokens, Hq, head_dim] tensor")
+        if q.dim() != 3 or q.shape[0] != T or q.shape[2] != D or q.stride(2) != 1 \
+                or q.stride(1) != D:
+            raise ValueError("q must be a [num_tokens, Hq, head_dim] tensor with packed heads")
         Hq = q.shape[1]
         if q_out is None:
-            q_out = torch.empty_like(q)
+            q_out = torch.empty((T, Hq, D), dtype=q.dtype, device=q.device)
     if kc.shape[2] != Hkv or kc.shape[3] != D:
         raise ValueError("kv_cache heads/head_dim do not match k")
     flags = 0
@@ -75,12 +76,13 @@ def kv_store_qknorm_rope(q: torch.Tensor | None, k: torch.Tensor, v: torch.Tenso
         require_dtype(positions, torch.int32, "positions")
     if wrap_negative_slots:
         flags |= _native.VJ_KV_WRAP_NEGATIVE
-    k_out = torch.empty_like(k) if return_k else None
+    k_out = torch.empty((T, Hkv, D), dtype=k.dtype, device=k.device) if return_k else None
     _native.call("vj_kv_store_qknorm_rope",
                  ptr(q), k.data_ptr(), v.data_ptr(), ptr(q_norm_weight if norm else None),
                  ptr(k_norm_weight if norm else None), ptr(positions if rope else None),
                  slot_mapping.data_ptr(), ptr(q_out), ptr(k_out), kc.data_ptr(), vc.data_ptr(),
-                 T, Hq, Hkv, D, nb, bs, sb, st, sh, float(eps), float(rope_theta), flags,
+                 T, Hq, Hkv, D, nb, bs, sb, st, sh, q.stride(0) if q is not None else 0,
+                 k.stride(0), v.stride(0), float(eps), float(rope_theta), flags,
                  stream_ptr(dev))
     if return_k:
         return q_out, k_out

@@ -105,7 +105,12 @@ class DeviceTables:
         arr = self._upload(np.concatenate([np.asarray(slots, np.int32),
                                            np.asarray(lens, np.int32)]))
         n = len(slots)
-        return arr[:n], arr[n:2 * n]
+        self._last = (arr[:n], arr[n:2 * n])
+        return self._last
+
+    def last_lists(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """Device (slots, lens) of the latest build_* call; valid until the next upload."""
+        return self._last
 
     def build_prefill(self, slots: list[int], lens: list[int], max_num_seqs: int,
                       width: int) -> PrefillMeta:
@@ -129,16 +134,24 @@ class DeviceTables:
                            d_lens.clone(), S, total)
 
     def build_decode(self, slots: list[int], lens: list[int], width: int,
-                     last_block_slot: bool = True) -> DecodeMeta:
+                     last_block_slot: bool = True, out: DecodeMeta | None = None) -> DecodeMeta:
+        """Decode metadata for len(slots) rows padded to a power of two; with
+        `out`, written into its (static, CUDA-graph) buffers of that bucket."""
         B = len(slots)
         bb = bucket_size(B)
         d_slots, d_lens = self._lists(slots, lens)
         dev = self.device
-        ids = torch.empty(bb, dtype=torch.int32, device=dev)
-        pos = torch.empty_like(ids)
-        sm = torch.empty_like(ids)
-        ctx = torch.empty_like(ids)
-        tables = torch.empty((bb, width), dtype=torch.int32, device=dev)
+        if out is not None:
+            if out.input_ids.numel() != bb or out.block_tables.shape[1] != width:
+                raise ValueError("static decode buffers do not match the batch bucket")
+            ids, pos, sm, ctx, tables = (out.input_ids, out.positions, out.slot_mapping,
+                                         out.context_lens, out.block_tables)
+        else:
+            ids = torch.empty(bb, dtype=torch.int32, device=dev)
+            pos = torch.empty_like(ids)
+            sm = torch.empty_like(ids)
+            ctx = torch.empty_like(ids)
+            tables = torch.empty((bb, width), dtype=torch.int32, device=dev)
         _native.call("vj_build_metadata", _native.VJ_META_DECODE, d_slots.data_ptr(),
                      d_lens.data_ptr(), B, self.tokens.data_ptr(), self.tokens.stride(0),
                      self.blocks.data_ptr(), self.num_blocks.data_ptr(), self.blocks.stride(0),
@@ -146,6 +159,9 @@ class DeviceTables:
                      _native.VJ_META_LAST_BLOCK_SLOT if last_block_slot else 0,
                      ids.data_ptr(), pos.data_ptr(), sm.data_ptr(), tables.data_ptr(), None,
                      ctx.data_ptr(), self.error.data_ptr(), stream_ptr(dev))
+        if out is not None:
+            out.num_seqs = B
+            return out
         return DecodeMeta(ids, pos, sm, tables, ctx, B)
 
     def argmax_append(self, logits: torch.Tensor, slots: torch.Tensor | None,

@@ -1,0 +1,256 @@
+"""Qwen3 decoder in torch around the sm_100a attention path.
+
+Dataflow per layer follows vllm-jax's vllm/model/qwen3.py:375-389
+(Qwen3DecoderLayer): input RMSNorm -> q/k/v projections -> per-head q/k
+RMSNorm -> RoPE -> KV store -> paged attention -> o_proj -> residual add ->
+post-attention RMSNorm -> SwiGLU MLP -> residual add; then the final norm and
+the (tied or untied) lm_head (:474-477). What changes:
+  * q/k norm, RoPE and the KV-slot scatter are one kernel (K3), prefill and
+    decode attention are K1 / K2 (libvjattn); dense GEMMs are cuBLAS.
+  * tensor parallelism by KV head: rank r holds q/k/v heads of KV heads
+    [r*Hkv/t, (r+1)*Hkv/t), the matching o_proj columns, 1/t of the MLP, and
+    one NCCL all-reduce follows o_proj and one follows down_proj (the
+    reference's Mesh annotations at qwen3.py:245-332 describe the same split).
+`attention(kv_cache, q, k, v, metadata)` keeps the reference boundary
+(qwen3.py:172-218) for callers that run their own projections.
+
+Weights are random (BASELINE: N(0, 0.02), seed 0): each tensor is drawn in a
+fixed order from a generator seeded with (seed, layer, name) and sliced for
+the rank, so every TP degree sees the same full model. RMSNorm scales are 1.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from ..kernels.decode_paged_attention import paged_decode
+from ..kernels.kv_store import kv_store_qknorm_rope, update_kv_cache
+from ..kernels.prefill_paged_attention import paged_prefill
+
+
+@dataclass
+class Qwen3Config:
+    vocab_size: int = 151936
+    hidden_size: int = 1024
+    intermediate_size: int = 3072
+    num_hidden_layers: int = 28
+    num_attention_heads: int = 16
+    num_key_value_heads: int = 8
+    head_dim: int = 128
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1_000_000.0
+    tie_word_embeddings: bool = True
+
+
+PRESETS = {
+    "Qwen3-0.6B": Qwen3Config(),
+    "Qwen3-8B": Qwen3Config(hidden_size=4096, intermediate_size=12288, num_hidden_layers=36,
+                            num_attention_heads=32, tie_word_embeddings=False),
+    "Qwen3-32B": Qwen3Config(hidden_size=5120, intermediate_size=25600, num_hidden_layers=64,
+                             num_attention_heads=64, tie_word_embeddings=False),
+}
+
+
+def get_config(name: str) -> Qwen3Config:
+    key = name.split("/")[-1]
+    if key not in PRESETS:
+        raise ValueError(f"unknown model {name!r}; known: {sorted(PRESETS)}")
+    return PRESETS[key]
+
+
+# ---------------------------------------------------------------------------
+# metadata structs of the attention boundary (vllm/model/qwen3.py:17-37)
+# ---------------------------------------------------------------------------
+@dataclass
+class DecodeAttentionMetadata:
+    input_positions: torch.Tensor
+    slot_mapping: torch.Tensor
+    block_tables: torch.Tensor
+    context_lens: torch.Tensor
+
+
+@dataclass
+class PrefillAttentionMetadata:
+    input_positions: torch.Tensor
+    slot_mapping: torch.Tensor
+    block_tables: torch.Tensor
+    cu_seqlens_q: torch.Tensor
+    cu_seqlens_k: torch.Tensor
+    max_seqlen_q: int
+    max_seqlen_k: int
+    max_seqlen_bucket: int
+    num_seqs: int | None = None          # sequences actually present (<= rows of block_tables)
+    context_lens: torch.Tensor | None = None  # keys per sequence (cached prefix + new)
+
+
+def attention(kv_cache: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+              metadata) -> tuple[torch.Tensor, torch.Tensor]:
+    """Drop-in for vllm/model/qwen3.py:172-218: store k/v (in place), then paged
+    prefill or decode attention. Returns (kv_cache, out [T, Hq, D])."""
+    update_kv_cache(kv_cache, metadata.slot_mapping, k, v)
+    if isinstance(metadata, PrefillAttentionMetadata):
+        S = metadata.num_seqs if metadata.num_seqs is not None else metadata.block_tables.shape[0]
+        out = paged_prefill(q, kv_cache, metadata.block_tables[:S], metadata.cu_seqlens_q[:S + 1],
+                            metadata.context_lens, max_seqlen_q=metadata.max_seqlen_bucket)
+    else:
+        out = paged_decode(q, kv_cache, metadata.block_tables, metadata.context_lens)
+    return kv_cache, out
+
+
+# ---------------------------------------------------------------------------
+# weights
+# ---------------------------------------------------------------------------
+def _draw(shape, seed: int, tag: int, gen_device: str, std: float = 0.02) -> torch.Tensor:
+    g = torch.Generator(device=gen_device)
+    g.manual_seed((seed * 1_000_003 + tag) & 0x7FFFFFFFFFFFFFFF)
+    return (torch.randn(shape, generator=g, device=gen_device, dtype=torch.float32) * std).to(
+        torch.bfloat16)
+
+
+@dataclass
+class LayerWeights:
+    w_qkv: torch.Tensor     # [(Hq_l + 2 Hkv_l) * D, hidden]
+    w_o: torch.Tensor       # [hidden, Hq_l * D]
+    w_gate_up: torch.Tensor  # [2 * I_l, hidden]
+    w_down: torch.Tensor    # [hidden, I_l]
+    ln1: torch.Tensor
+    ln2: torch.Tensor
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+
+
+class Qwen3Weights:
+    """Random-init weights, sharded for (tp_rank, tp_size). Parameter order and
+    the per-tensor seeds are fixed, so the full model is the same at every TP
+    degree and on every generator device of the same kind."""
+
+    def __init__(self, cfg: Qwen3Config, device: torch.device, seed: int = 0, tp_rank: int = 0,
+                 tp_size: int = 1, gen_device: str | None = None):
+        H, D, I = cfg.hidden_size, cfg.head_dim, cfg.intermediate_size
+        Hq, Hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        if Hkv % tp_size or I % tp_size:
+            raise ValueError(f"tensor_parallel_size {tp_size} must divide {Hkv} KV heads and "
+                             f"intermediate {I}")
+        gen = gen_device or ("cuda" if device.type == "cuda" else "cpu")
+        hq_l, hkv_l, i_l = Hq // tp_size, Hkv // tp_size, I // tp_size
+        r = tp_rank
+        self.cfg = cfg
+        self.tp_rank, self.tp_size = tp_rank, tp_size
+        one = torch.ones(H, dtype=torch.bfloat16, device=device)
+        oned = torch.ones(D, dtype=torch.bfloat16, device=device)
+        self.embed = _draw((cfg.vocab_size, H), seed, 1, gen).to(device)
+        self.layers: list[LayerWeights] = []
+        for layer in range(cfg.num_hidden_layers):
+            base = 100 + 16 * layer
+            wq = _draw((Hq * D, H), seed, base + 0, gen)
+            wk = _draw((Hkv * D, H), seed, base + 1, gen)
+            wv = _draw((Hkv * D, H), seed, base + 2, gen)
+            wo = _draw((H, Hq * D), seed, base + 3, gen)
+            wg = _draw((I, H), seed, base + 4, gen)
+            wu = _draw((I, H), seed, base + 5, gen)
+            wd = _draw((H, I), seed, base + 6, gen)
+            qs = slice(r * hq_l * D, (r + 1) * hq_l * D)
+            ks = slice(r * hkv_l * D, (r + 1) * hkv_l * D)
+            isl = slice(r * i_l, (r + 1) * i_l)
+            self.layers.append(LayerWeights(
+                w_qkv=torch.cat([wq[qs], wk[ks], wv[ks]]).to(device).contiguous(),
+                w_o=wo[:, qs].to(device).contiguous(),
+                w_gate_up=torch.cat([wg[isl], wu[isl]]).to(device).contiguous(),
+                w_down=wd[:, isl].to(device).contiguous(),
+                ln1=one, ln2=one, q_norm=oned, k_norm=oned))
+            del wq, wk, wv, wo, wg, wu, wd
+        self.norm = one
+        self.lm_head = (self.embed if cfg.tie_word_embeddings
+                        else _draw((cfg.vocab_size, H), seed, 2, gen).to(device))
+
+    def full_numpy(self):
+        """Every tensor as float32 numpy (unsharded models only; for the oracle)."""
+        assert self.tp_size == 1
+        f = lambda t: t.float().cpu().numpy()
+        return {"embed": f(self.embed), "norm": f(self.norm), "lm_head": f(self.lm_head),
+                "layers": [{k: f(getattr(lw, k)) for k in LayerWeights.__dataclass_fields__}
+                           for lw in self.layers]}
+
+
+# ---------------------------------------------------------------------------
+# model
+# ---------------------------------------------------------------------------
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """flax RMSNorm semantics: fp32 statistics, bf16(x * (rsqrt(ms + eps) * w))."""
+    xf = x.float()
+    mul = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+    return (xf * mul).to(torch.bfloat16)
+
+
+class Qwen3Model:
+    """Forward passes of one rank. kv_caches[l]: (2, num_blocks, bs, Hkv_l, D) bf16."""
+
+    def __init__(self, weights: Qwen3Weights, process_group=None):
+        self.w = weights
+        self.cfg = weights.cfg
+        self.pg = process_group
+        c = self.cfg
+        self.hq = c.num_attention_heads // weights.tp_size
+        self.hkv = c.num_key_value_heads // weights.tp_size
+        self.d = c.head_dim
+        self.scale = 1.0 / math.sqrt(c.head_dim)
+
+    def _all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        if self.pg is not None and self.w.tp_size > 1:
+            torch.distributed.all_reduce(x, group=self.pg)
+        return x
+
+    def _layer(self, l: int, x: torch.Tensor, kv_cache: torch.Tensor, meta, attn_fn):
+        lw = self.w.layers[l]
+        c = self.cfg
+        T = x.shape[0]
+        h = rms_norm(x, lw.ln1, c.rms_norm_eps)
+        qkv = F.linear(h, lw.w_qkv)
+        q, k, v = torch.split(qkv, [self.hq * self.d, self.hkv * self.d, self.hkv * self.d], -1)
+        q = kv_store_qknorm_rope(q.view(T, self.hq, self.d), k.view(T, self.hkv, self.d),
+                                 v.view(T, self.hkv, self.d), kv_cache,
+                                 meta.slot_mapping, meta.positions, lw.q_norm, lw.k_norm,
+                                 eps=c.rms_norm_eps, rope_theta=c.rope_theta)
+        o = attn_fn(q, kv_cache).reshape(T, self.hq * self.d)
+        o = self._all_reduce(F.linear(o, lw.w_o))
+        x = x + o                                   # attn_output += x (bf16)
+        h = rms_norm(x, lw.ln2, c.rms_norm_eps)
+        gu = F.linear(h, lw.w_gate_up)
+        g, u = gu.chunk(2, dim=-1)
+        m = F.silu(g) * u
+        d = self._all_reduce(F.linear(m, lw.w_down))
+        return x + d
+
+    def embed(self, input_ids: torch.Tensor) -> torch.Tensor:
+        return F.embedding(input_ids.long(), self.w.embed)
+
+    def forward_prefill(self, meta, kv_caches: list[torch.Tensor]) -> torch.Tensor:
+        """Packed prefill of meta.num_tokens tokens (bucket-padded); writes the
+        KV caches and returns the final hidden states (the reference computes
+        no logits in prefill, model_runner.py:41-59)."""
+        x = self.embed(meta.input_ids)
+        S = meta.num_seqs
+
+        def attn(q, kv):
+            return paged_prefill(q, kv, meta.block_tables[:S], meta.cu_seqlens_q[:S + 1],
+                                 getattr(meta, "context_lens", None),
+                                 max_seqlen_q=meta.max_seqlen_bucket, scale=self.scale)
+
+        for l in range(self.cfg.num_hidden_layers):
+            x = self._layer(l, x, kv_caches[l], meta, attn)
+        return rms_norm(x, self.w.norm, self.cfg.rms_norm_eps)
+
+    def forward_decode(self, meta, kv_caches: list[torch.Tensor]) -> torch.Tensor:
+        """One token per row; returns bf16 logits [rows, vocab]."""
+        x = self.embed(meta.input_ids)
+
+        def attn(q, kv):
+            return paged_decode(q, kv, meta.block_tables, meta.context_lens, self.scale)
+
+        for l in range(self.cfg.num_hidden_layers):
+            x = self._layer(l, x, kv_caches[l], meta, attn)
+        x = rms_norm(x, self.w.norm, self.cfg.rms_norm_eps)
+        return F.linear(x, self.w.lm_head)           # compute_logits (qwen3.py:474-477)

@@ -1,0 +1,139 @@
+"""Continuous-batching engine with vllm-jax's API (vllm/src/engine.py:13-75).
+
+`Engine(config).generate(prompts, **sampling_kwargs)` runs the reference's
+loop: schedule -> model step -> postprocess until every request finished.
+Prompts may be token-id lists (no tokenizer is needed) or strings, which
+require a `tokenizer` object with encode/decode (HF weights and tokenizers
+are not downloadable here, so the model is the random-init architecture the
+benchmarks name). `LLM` is an alias: the reference has no class of that name
+and north_star's LLM.generate maps to Engine.generate.
+
+Tensor parallelism: launch one process per GPU (torchrun) with
+config.tensor_parallel_size = world size; every rank runs the same
+deterministic scheduler on the same requests, so the batches agree and no
+host broadcast is needed; the model all-reduces after o_proj and down_proj.
+"""
+from __future__ import annotations
+
+import dataclasses
+import os
+import time
+
+import torch
+
+from ..config import Config
+from ..model.qwen3 import Qwen3Config, Qwen3Weights, get_config
+from ..sampling_params import SamplingParams
+from .kv_cache_manager import KVCacheManager
+from .model_runner import ModelRunner, kv_cache_bytes_per_block
+from .request import Request
+from .scheduler import Scheduler
+
+
+class Engine:
+
+    def __init__(self, config: Config, device: torch.device | None = None, *,
+                 model_config: Qwen3Config | None = None, tokenizer=None, seed: int = 0,
+                 eos_token_id: int | None = 151645, process_group=None,
+                 weights: Qwen3Weights | None = None, max_slots: int = 4096,
+                 use_cuda_graphs: bool = True):
+        self.config = config
+        self.tokenizer = tokenizer
+        self.eos_token_id = (tokenizer.eos_token_id if tokenizer is not None
+                             else eos_token_id)
+        self.tp_size = config.tensor_parallel_size
+        self.tp_rank = 0
+        if self.tp_size > 1:
+            if not torch.distributed.is_initialized():
+                raise RuntimeError("tensor_parallel_size > 1 needs torch.distributed "
+                                   "initialised (one process per GPU)")
+            self.tp_rank = torch.distributed.get_rank(process_group)
+            if torch.distributed.get_world_size(process_group) != self.tp_size:
+                raise ValueError("tensor_parallel_size must equal the process group size")
+        if device is None:
+            device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        torch.cuda.set_device(device)
+        self.device = device
+        self.mcfg = model_config or get_config(config.model)
+        self.weights = weights or Qwen3Weights(self.mcfg, device, seed, self.tp_rank,
+                                               self.tp_size)
+        num_blocks = config.num_blocks
+        if num_blocks <= 0:
+            free, _ = torch.cuda.mem_get_info(device)
+            per = kv_cache_bytes_per_block(self.mcfg, config.block_size, self.tp_size)
+            num_blocks = int(free * config.gpu_memory_utilization) // per
+            if self.tp_size > 1:   # every rank must agree on the pool size
+                t = torch.tensor([num_blocks], device=device)
+                torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN,
+                                             group=process_group)
+                num_blocks = int(t.item())
+            self.config = config = dataclasses.replace(config, num_blocks=num_blocks)
+        self.kv = KVCacheManager(num_blocks, config.block_size)
+        self.scheduler = Scheduler(config, self.kv)
+        self.runner = ModelRunner(config, self.mcfg, self.kv, device, tp_rank=self.tp_rank,
+                                  tp_size=self.tp_size, process_group=process_group,
+                                  weights=self.weights, max_slots=max_slots,
+                                  use_cuda_graphs=use_cuda_graphs)
+        self.live: dict[int, Request] = {}
+        self.stats = {"steps": 0, "decode_tokens": 0, "prefill_tokens": 0}
+
+    # ---------------------------------------------------------------- requests
+    def preprocess(self, prompt) -> list[int]:
+        if isinstance(prompt, str):
+            if self.tokenizer is None:
+                raise ValueError("string prompts need a tokenizer; pass token-id lists")
+            return list(self.tokenizer.encode(prompt))
+        return [int(t) for t in prompt]
+
+    def add_request(self, request: Request) -> None:
+        if len(request) + request.max_new_tokens > self.config.max_len:
+            raise ValueError(f"request {request.id}: {len(request)} prompt + "
+                             f"{request.max_new_tokens} new tokens exceed max_model_len "
+                             f"{self.config.max_len}")
+        self.live[request.id] = request
+        self.scheduler.add(request)
+
+    # ---------------------------------------------------------------- loop
+    def step(self) -> list[tuple[int, int]]:
+        decode, prefill = self.scheduler.schedule()
+        tokens = self.runner.run(decode, prefill, self.live)
+        self.scheduler.postprocess(decode, tokens)
+        self.stats["steps"] += 1
+        self.stats["decode_tokens"] += len(decode)
+        self.stats["prefill_tokens"] += sum(len(r) for r in prefill)
+        done = []
+        for r in decode:
+            if r.is_finished():
+                done.append((r.id, r.num_completion_tokens))
+                self.runner.release(r)
+                del self.live[r.id]
+        return done
+
+    def generate(self, prompts, sampling_params: SamplingParams | list | None = None,
+                 **kwargs):
+        """vllm/src/engine.py:45-75. Returns, per prompt, the completion text
+        (with a tokenizer) or the list of completion token ids."""
+        if sampling_params is None:
+            names = {f.name for f in dataclasses.fields(SamplingParams)}
+            sampling_params = SamplingParams(**{k: v for k, v in kwargs.items() if k in names})
+        params = (sampling_params if isinstance(sampling_params, list)
+                  else [sampling_params] * len(prompts))
+        for sp in params:
+            if sp.temperature > 0:
+                raise NotImplementedError("only greedy decoding (temperature <= 0) is built; "
+                                          "the top-k/top-p sampler is out of scope")
+        reqs = []
+        for p, sp in zip(prompts, params):
+            r = Request(self.preprocess(p), sp, self.eos_token_id)
+            reqs.append(r)
+            self.add_request(r)
+        while not self.scheduler.is_finished():
+            self.step()
+        outs = []
+        for r in reqs:
+            comp = r.token_ids[r.num_prompt_tokens:]
+            outs.append(self.tokenizer.decode(comp) if self.tokenizer is not None else comp)
+        return outs
+
+
+LLM = Engine

@@ -1,0 +1,155 @@
+"""Model runner: device-resident batch state, GPU metadata, CUDA-graph decode.
+
+Counterpart of vllm-jax's vllm/src/model_runner.py (ModelRunner.run,
+:310-333). Per engine step the host sends only what changed: the token ids
+of newly admitted requests and the block lists the KV manager touched (one
+small upload each), plus the scheduled (slot, length) pairs. The metadata
+arrays of prepare_prefill / prepare_decode are then built on the GPU (K4),
+the sampled tokens are written into the device token table by the argmax
+kernel, and one device->host copy of [batch] int32 per step returns them to
+the scheduler. Decode steps replay a CUDA graph captured per power-of-two
+batch bucket (the reference's jit buckets, model_runner.py:125-183).
+"""
+from __future__ import annotations
+
+import torch
+
+from ..config import Config
+from ..kernels.metadata import DecodeMeta, DeviceTables, bucket_size
+from ..model.qwen3 import Qwen3Config, Qwen3Model, Qwen3Weights
+from .kv_cache_manager import KVCacheManager
+from .request import Request
+
+
+def kv_cache_bytes_per_block(mcfg: Qwen3Config, block_size: int, tp_size: int) -> int:
+    return (mcfg.num_hidden_layers * 2 * block_size * (mcfg.num_key_value_heads // tp_size)
+            * mcfg.head_dim * 2)
+
+
+class ModelRunner:
+
+    def __init__(self, config: Config, model_cfg: Qwen3Config, kv_cache_manager: KVCacheManager,
+                 device: torch.device, *, tp_rank: int = 0, tp_size: int = 1,
+                 process_group=None, seed: int = 0, weights: Qwen3Weights | None = None,
+                 max_slots: int = 1024, use_cuda_graphs: bool = True):
+        self.config = config
+        self.mcfg = model_cfg
+        self.kv = kv_cache_manager
+        self.device = device
+        self.block_size = config.block_size
+        self.width = config.max_blocks_per_seq
+        self.weights = weights or Qwen3Weights(model_cfg, device, seed, tp_rank, tp_size)
+        self.model = Qwen3Model(self.weights, process_group)
+        hkv = model_cfg.num_key_value_heads // tp_size
+        shape = (2, kv_cache_manager.num_blocks, config.block_size, hkv, model_cfg.head_dim)
+        # zero-initialised like the reference's pool (model_runner.py:190-199)
+        self.kv_caches = [torch.zeros(shape, dtype=torch.bfloat16, device=device)
+                          for _ in range(model_cfg.num_hidden_layers)]
+        self.tables = DeviceTables(max_slots, config.max_len, self.width, config.block_size,
+                                   device)
+        self.free_slots = list(range(max_slots - 1, -1, -1))
+        self.use_cuda_graphs = use_cuda_graphs
+        self.graphs: dict[int, tuple[torch.cuda.CUDAGraph, DecodeMeta, torch.Tensor]] = {}
+        self._tok_host = torch.empty(max(config.max_num_seqs, 1), dtype=torch.int32).pin_memory()
+
+    # ------------------------------------------------------------------ state sync
+    def _assign_slot(self, request: Request) -> int:
+        if request.slot < 0:
+            if not self.free_slots:
+                raise RuntimeError("no free request slot: raise max_slots")
+            request.slot = self.free_slots.pop()
+            # the device token row gets every token known now; later tokens are
+            # appended on the device by the sampler
+            self.tables.set_tokens([(request.slot, 0, list(request.token_ids))])
+        return request.slot
+
+    def release(self, request: Request) -> None:
+        if request.slot >= 0:
+            self.free_slots.append(request.slot)
+            request.slot = -1
+
+    def _sync_blocks(self, requests: dict[int, Request]) -> None:
+        rows = []
+        for rid in sorted(self.kv.dirty):
+            r = requests.get(rid)
+            if r is not None and r.slot >= 0:
+                rows.append((r.slot, self.kv.block_ids(r)))
+        self.kv.dirty.clear()
+        self.tables.set_blocks(rows)
+
+    # ------------------------------------------------------------------ decode
+    def _decode_graph(self, bb: int):
+        if bb in self.graphs:
+            return self.graphs[bb]
+        dev = self.device
+        meta = DecodeMeta(torch.zeros(bb, dtype=torch.int32, device=dev),
+                          torch.zeros(bb, dtype=torch.int32, device=dev),
+                          torch.full((bb,), -1, dtype=torch.int32, device=dev),
+                          torch.full((bb, self.width), -1, dtype=torch.int32, device=dev),
+                          torch.zeros(bb, dtype=torch.int32, device=dev), bb)
+        # warm up eagerly (sizes workspaces, cuBLAS handles), then capture
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            self.model.forward_decode(meta, self.kv_caches)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            logits = self.model.forward_decode(meta, self.kv_caches)
+        self.graphs[bb] = (graph, meta, logits)
+        return self.graphs[bb]
+
+    def capture_all(self, max_batch: int) -> None:
+        b = 1
+        while True:
+            self._decode_graph(b)
+            if b >= max_batch:
+                break
+            b *= 2
+
+    def decode(self, requests: list[Request]) -> list[int]:
+        slots = [r.slot for r in requests]
+        lens = [len(r) for r in requests]
+        B = len(requests)
+        bb = bucket_size(B)
+        if self.use_cuda_graphs:
+            graph, meta, logits = self._decode_graph(bb)
+            self.tables.build_decode(slots, lens, self.width, out=meta,
+                                     last_block_slot=self.config.compat)
+            graph.replay()
+        else:
+            meta = self.tables.build_decode(slots, lens, self.width,
+                                            last_block_slot=self.config.compat)
+            logits = self.model.forward_decode(meta, self.kv_caches)
+        d_slots, d_lens = self.tables.last_lists()
+        toks = self.tables.argmax_append(logits[:B], d_slots, d_lens)
+        host = self._tok_host if B <= self._tok_host.numel() else torch.empty(
+            B, dtype=torch.int32).pin_memory()
+        host[:B].copy_(toks, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return host[:B].tolist()
+
+    # ------------------------------------------------------------------ prefill
+    def prefill(self, requests: list[Request]) -> None:
+        meta = self.tables.build_prefill([r.slot for r in requests], [len(r) for r in requests],
+                                         self.config.max_num_seqs, self.width)
+        self.model.forward_prefill(meta, self.kv_caches)
+
+    # ------------------------------------------------------------------ step
+    def run(self, decode_requests: list[Request], prefill_requests: list[Request],
+            live: dict[int, Request]) -> list[int]:
+        """One engine step (model_runner.py:310-333): decode batch first (its
+        tokens are returned and appended to the requests), then the prefill
+        batch (KV only; its first token comes from the next step's decode)."""
+        for r in prefill_requests:
+            self._assign_slot(r)
+        self._sync_blocks(live)
+        out: list[int] = []
+        if decode_requests:
+            out = self.decode(decode_requests)
+            for r, t in zip(decode_requests, out):
+                r.token_ids.append(t)
+                r.num_completion_tokens += 1
+        if prefill_requests:
+            self.prefill(prefill_requests)
+        return out
