@@ -567,13 +567,125 @@ def run_reference(args, rank, world):
     pool.terminate()
 
 
+# C4: Qwen3-8B continuous batching
+C4 = dict(model="Qwen3-8B", num_requests=512, prompt_min=100, prompt_max=1024, out_min=100,
+          out_max=1024, max_num_batched_tokens=16384, max_num_seqs=512, seed=0)
+
+
+def c4_requests(cfg=C4, vocab=151936):
+    rng = np.random.default_rng(cfg["seed"])
+    n = cfg["num_requests"]
+    plen = rng.integers(cfg["prompt_min"], cfg["prompt_max"] + 1, n)
+    olen = rng.integers(cfg["out_min"], cfg["out_max"] + 1, n)
+    prompts = [rng.integers(0, vocab, int(L)).tolist() for L in plen]
+    return prompts, [int(x) for x in olen]
+
+
+def run_e2e(args, rank, world, local_rank):
+    """C4 end to end: output tokens/s of Engine.generate over 512 requests
+    (random prompts and output lengths, greedy, ignore_eos), tensor parallel
+    over `world` GPUs (KV heads and MLP split, NCCL all-reduce after o_proj and
+    down_proj). The timed region is the whole generate() call: host scheduling,
+    metadata uploads, prefill and CUDA-graph decode steps, token D2H."""
+    import torch
+    import torch.distributed as dist
+    from vllm_b200 import Config, SamplingParams, _native
+    from vllm_b200.model.qwen3 import get_config
+    from vllm_b200.src.engine import Engine
+
+    cfg = dict(C4)
+    if args.model:
+        cfg["model"] = args.model
+    if args.batch is not None:
+        cfg["num_requests"] = args.batch
+    if args.max_num_seqs:
+        cfg["max_num_seqs"] = args.max_num_seqs
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    mcfg = get_config(cfg["model"])
+    prompts, outs = c4_requests(cfg, mcfg.vocab_size)
+    max_len = max(len(p) + o for p, o in zip(prompts, outs))
+    econf = Config(model=cfg["model"], max_num_batched_tokens=cfg["max_num_batched_tokens"],
+                   max_num_seqs=cfg["max_num_seqs"], num_blocks=0, block_size=16,
+                   tensor_parallel_size=world, gpu_memory_utilization=0.9,
+                   max_model_len=((max_len + 15) // 16) * 16, compat=False)
+    pg = dist.group.WORLD if world > 1 else None
+    eng = Engine(econf, dev, seed=0, process_group=pg, max_slots=cfg["num_requests"] + 8)
+    eng.runner.capture_all(cfg["max_num_seqs"])
+    # warm-up: a few short requests (cuBLAS heuristics, prefill kernels)
+    for _ in range(max(args.warmup, 1)):
+        eng.generate(prompts[:8], SamplingParams(temperature=0, max_new_tokens=4,
+                                                 ignore_eos=True))
+    params = [SamplingParams(temperature=0, max_new_tokens=o, ignore_eos=True) for o in outs]
+    times, stats = [], []
+    launches0 = _native.launch_count
+    for _ in range(args.steps):
+        for k in eng.stats:
+            eng.stats[k] = 0 if isinstance(eng.stats[k], int) else 0.0
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        with ClockSampler(local_rank) as clk:
+            t0 = time.perf_counter()
+            res = eng.generate(prompts, params)
+            torch.cuda.synchronize()
+            t1 = time.perf_counter()
+        times.append(t1 - t0)
+        stats.append(dict(eng.stats))
+        assert [len(r) for r in res] == outs
+    t = torch.tensor([max(times)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    wall = float(t.item())
+    if rank != 0:
+        return
+    value = sum(outs) / wall
+    st = stats[-1]
+    peaks, src = load_peaks()
+    # decode-step roofline: weights of one rank + K/V of every context token per step
+    wbytes = sum(p.numel() * 2 for lw in eng.weights.layers for p in
+                 (lw.w_qkv, lw.w_o, lw.w_gate_up, lw.w_down)) + eng.weights.lm_head.numel() * 2
+    kvb = mcfg.num_hidden_layers * 2 * (mcfg.num_key_value_heads // world) * mcfg.head_dim * 2
+    dec_bytes = st["decode_steps"] * wbytes + st["decode_ctx_tokens"] * kvb
+    achieved = dec_bytes / max(st["decode_s"], 1e-9) / 1e9
+    line = {
+        "metric": f"output tok/s {cfg['model']} continuous batching (C4: "
+                  f"{cfg['num_requests']} requests, prompts U[100,1024], outputs U[100,1024])",
+        "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 1), "ms_per_step": round(wall * 1e3, 1),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random token ids and lengths; random-init N(0,0.02) weights)",
+        "config": {"workload": "C4 end-to-end continuous batching", "model": cfg["model"],
+                   "num_requests": cfg["num_requests"], "output_tokens": sum(outs),
+                   "max_num_batched_tokens": cfg["max_num_batched_tokens"],
+                   "max_num_seqs": cfg["max_num_seqs"], "num_blocks": eng.config.num_blocks,
+                   "parallelism": f"tp{world}" if world > 1 else "single GPU",
+                   "engine_steps": st["steps"], "decode_steps": st["decode_steps"],
+                   "prefill_s": round(st["prefill_s"], 3), "decode_s": round(st["decode_s"], 3),
+                   "l2": "decode steps stream all weights + KV (> L2)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "peak_source": f"{src} hbm_gbs",
+                     "kernel": "decode step (weights/TP + KV bytes per step / host-timed step)",
+                     "traffic": None},
+        "e2e": {"value": round(value, 1), "unit": "tok/s",
+                "h2d_bytes_per_step": st["h2d_bytes"] // max(st["steps"], 1),
+                "d2h_bytes_per_step": st["d2h_bytes"] // max(st["steps"], 1)},
+        "gpu_launches": _native.launch_count - launches0,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "prefill", "e2e"], default="decode")
+    ap.add_argument("--model", default=None, help="e2e: model preset (default Qwen3-8B)")
+    ap.add_argument("--max-num-seqs", type=int, default=None, help="e2e: scheduler seats")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--ref-budget", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -603,6 +715,10 @@ def main():
     try:
         if args.workload == "prefill":
             run_prefill(args, rank, world, local_rank)
+        elif args.workload == "e2e":
+            if args.steps > 3:
+                args.steps = 1      # one generate() of the whole C4 request set per step
+            run_e2e(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:

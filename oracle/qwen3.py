@@ -134,7 +134,8 @@ class OracleQwen3:
 def greedy_replay(model: OracleQwen3, trace: dict, prompts: list[list[int]]):
     """Replay the scheduled steps of a golden host trace (block tables, slots
     and positions depend only on lengths there) with the oracle's own tokens.
-    Returns (tokens per request id, per decode step (top1, top2 gap) per row)."""
+    Returns (tokens per request id, per decode step a list of (top id, top
+    logit, top-2 logit gap) per scheduled row)."""
     tokens = {i: list(p) for i, p in enumerate(prompts)}
     gaps = []
     for st in trace["steps"]:
@@ -149,7 +150,7 @@ def greedy_replay(model: OracleQwen3, trace: dict, prompts: list[list[int]]):
                 lg = logits[row]
                 top = int(np.argmax(lg))
                 srt = np.sort(lg)
-                step.append((top, float(srt[-1] - srt[-2])))
+                step.append((top, float(srt[-1]), float(srt[-1] - srt[-2])))
                 tokens[r].append(top)
             gaps.append(step)
         if "prefill" in st:

@@ -72,10 +72,11 @@ def test_c1_greedy_tokens_vs_oracle(c1_run):
           f"first divergence {first_div}")
     if first_div is not None:
         r, step = first_div
-        top, gap = gaps[step][r]
-        ulp = 2.0 ** (math.floor(math.log2(abs(max(1e-3, top)))) - 7) if top else 2 ** -7
-        lg = max(abs(x[0]) for x in gaps[step])
-        assert gap <= 4 * 2.0 ** (math.floor(math.log2(max(lg, 1.0))) - 7) + 1e-6, (
+        _, top_logit, gap = gaps[step][r]
+        # a few bf16 ulps at the magnitude of the top logit (logits are bf16)
+        ulp = 2.0 ** (math.floor(math.log2(max(abs(top_logit), 2.0 ** -10))) - 7)
+        print(f"oracle top logit {top_logit:.4f}, top-2 gap {gap:.4f} ({gap / ulp:.1f} ulp)")
+        assert gap <= 4 * ulp + 1e-9, (
             f"request {r} diverged at step {step} with an oracle top-2 gap of {gap}")
     assert n_match >= 64
 
@@ -122,8 +123,8 @@ def test_attention_boundary_reference_signature():
     qd = bf16(rng.standard_normal((2, Hq, D)))
     kd = bf16(rng.standard_normal((2, Hkv, D)))
     vd = bf16(rng.standard_normal((2, Hkv, D)))
-    dslots = np.array([3 * bs + 4 if False else blocks[0][20 // bs] * bs + 20 % bs,
-                       blocks[1][37 // bs] * bs + 37 % bs], np.int32)
+    dslots = np.array([blocks[0][20 // bs] * bs + 20 % bs, blocks[1][37 // bs] * bs + 37 % bs],
+                      np.int32)
     okv.update_kv_cache(kc, vc, dslots, kd, vd)
     ctx = np.array([21, 38], np.int32)
     ref = oatt.decode_attention(qd, kc, vc, bt[:2], ctx, 1 / math.sqrt(D))

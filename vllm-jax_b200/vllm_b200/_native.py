@@ -105,5 +105,14 @@ def check(status: int) -> None:
         raise VJError(status, msg)
 
 
+# kernels launched by one successful call of each entry point
+KERNELS_PER_CALL = {"vj_paged_decode": 3, "vj_paged_decode_noalloc": 3, "vj_paged_prefill": 2}
+launch_count = 0
+
+
 def call(name: str, *args) -> None:
+    """Call an entry point, raise on a nonzero status, count its kernel launches
+    (a CUDA graph replay adds the launches counted while it was captured)."""
+    global launch_count
     check(getattr(load(), name)(*args))
+    launch_count += KERNELS_PER_CALL.get(name, 1)

@@ -75,7 +75,9 @@ class Engine:
                                   weights=self.weights, max_slots=max_slots,
                                   use_cuda_graphs=use_cuda_graphs)
         self.live: dict[int, Request] = {}
-        self.stats = {"steps": 0, "decode_tokens": 0, "prefill_tokens": 0}
+        self.stats = {"steps": 0, "decode_tokens": 0, "prefill_tokens": 0, "decode_steps": 0,
+                      "decode_s": 0.0, "prefill_s": 0.0, "decode_ctx_tokens": 0,
+                      "h2d_bytes": 0, "d2h_bytes": 0}
 
     # ---------------------------------------------------------------- requests
     def preprocess(self, prompt) -> list[int]:
@@ -96,11 +98,14 @@ class Engine:
     # ---------------------------------------------------------------- loop
     def step(self) -> list[tuple[int, int]]:
         decode, prefill = self.scheduler.schedule()
-        tokens = self.runner.run(decode, prefill, self.live)
+        st = self.stats
+        st["decode_ctx_tokens"] += sum(len(r) for r in decode)
+        tokens = self.runner.run(decode, prefill, self.live, st)
         self.scheduler.postprocess(decode, tokens)
-        self.stats["steps"] += 1
-        self.stats["decode_tokens"] += len(decode)
-        self.stats["prefill_tokens"] += sum(len(r) for r in prefill)
+        st["steps"] += 1
+        st["decode_tokens"] += len(decode)
+        st["decode_steps"] += 1 if decode else 0
+        st["prefill_tokens"] += sum(len(r) for r in prefill)
         done = []
         for r in decode:
             if r.is_finished():

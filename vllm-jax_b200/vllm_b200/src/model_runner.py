@@ -12,8 +12,11 @@ batch bucket (the reference's jit buckets, model_runner.py:125-183).
 """
 from __future__ import annotations
 
+import time
+
 import torch
 
+from .. import _native
 from ..config import Config
 from ..kernels.metadata import DecodeMeta, DeviceTables, bucket_size
 from ..model.qwen3 import Qwen3Config, Qwen3Model, Qwen3Weights
@@ -50,6 +53,7 @@ class ModelRunner:
         self.free_slots = list(range(max_slots - 1, -1, -1))
         self.use_cuda_graphs = use_cuda_graphs
         self.graphs: dict[int, tuple[torch.cuda.CUDAGraph, DecodeMeta, torch.Tensor]] = {}
+        self.graph_launches: dict[int, int] = {}
         self._tok_host = torch.empty(max(config.max_num_seqs, 1), dtype=torch.int32).pin_memory()
 
     # ------------------------------------------------------------------ state sync
@@ -94,8 +98,11 @@ class ModelRunner:
             self.model.forward_decode(meta, self.kv_caches)
         torch.cuda.current_stream(dev).wait_stream(s)
         graph = torch.cuda.CUDAGraph()
+        before = _native.launch_count
         with torch.cuda.graph(graph):
             logits = self.model.forward_decode(meta, self.kv_caches)
+        self.graph_launches[bb] = _native.launch_count - before
+        _native.launch_count = before
         self.graphs[bb] = (graph, meta, logits)
         return self.graphs[bb]
 
@@ -117,6 +124,7 @@ class ModelRunner:
             self.tables.build_decode(slots, lens, self.width, out=meta,
                                      last_block_slot=self.config.compat)
             graph.replay()
+            _native.launch_count += self.graph_launches[bb]
         else:
             meta = self.tables.build_decode(slots, lens, self.width,
                                             last_block_slot=self.config.compat)
@@ -137,19 +145,31 @@ class ModelRunner:
 
     # ------------------------------------------------------------------ step
     def run(self, decode_requests: list[Request], prefill_requests: list[Request],
-            live: dict[int, Request]) -> list[int]:
+            live: dict[int, Request], stats: dict | None = None) -> list[int]:
         """One engine step (model_runner.py:310-333): decode batch first (its
         tokens are returned and appended to the requests), then the prefill
         batch (KV only; its first token comes from the next step's decode)."""
+        t0 = time.perf_counter()
         for r in prefill_requests:
+            if r.slot < 0 and stats is not None:
+                stats["h2d_bytes"] += 4 * len(r.token_ids)
             self._assign_slot(r)
         self._sync_blocks(live)
         out: list[int] = []
         if decode_requests:
-            out = self.decode(decode_requests)
+            out = self.decode(decode_requests)   # ends with the D2H of the tokens
             for r, t in zip(decode_requests, out):
                 r.token_ids.append(t)
                 r.num_completion_tokens += 1
+        t1 = time.perf_counter()
         if prefill_requests:
             self.prefill(prefill_requests)
+        if stats is not None:
+            stats["h2d_bytes"] += 8 * (len(decode_requests) + len(prefill_requests))
+            stats["d2h_bytes"] += 4 * len(decode_requests)
+            if decode_requests:
+                stats["decode_s"] += t1 - t0
+            if prefill_requests:
+                torch.cuda.current_stream(self.device).synchronize()
+                stats["prefill_s"] += time.perf_counter() - t1
         return out
