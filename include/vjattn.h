@@ -184,6 +184,21 @@ VJ_API vj_status vj_paged_prefill(
     int32_t *error_flag, cudaStream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Fused decoder-layer epilogues (vllm/model/qwen3.py:375-389, :337-341).
+ * vj_add_rmsnorm: r = bf16(x + residual) (stored to residual_out when given;
+ * residual may be NULL for a plain norm), y = bf16(r * (rsqrt(mean(r^2) +
+ * eps) * weight)) with fp32 statistics; rows x hidden bf16, hidden % 8 == 0,
+ * hidden <= 8192. vj_silu_mul: out[t, i] = bf16(bf16(silu(g)) * u) for
+ * gate_up = [g | u] of shape [rows, 2 * inter].
+ * ------------------------------------------------------------------------- */
+VJ_API vj_status vj_add_rmsnorm(const void *x, const void *residual,
+                                const void *weight, void *residual_out, void *y,
+                                int64_t rows, int32_t hidden, float eps,
+                                cudaStream_t stream);
+VJ_API vj_status vj_silu_mul(const void *gate_up, void *out, int64_t rows,
+                             int32_t inter, cudaStream_t stream);
+
+/* ---------------------------------------------------------------------------
  * K4: batch metadata built on the GPU from device-resident engine state.
  * Replaces vllm/src/model_runner.py:204-214 (pad_block_tables), :217-266
  * (prepare_prefill) and :268-301 (prepare_decode); the outputs equal the

@@ -7,7 +7,7 @@
 //                                pairs (x[2i], x[2i+1]), bf16 cos/sin)
 //   vllm/model/qwen3.py:105-111  _update_kv_cache (.at[slot].set, mode=drop)
 //
-// Work split: a CTA owns kTokPerCta tokens. It first builds the bf16 cos/sin
+// Work split: a CTA owns kTokPerCta (2) tokens. It first builds the bf16 cos/sin
 // table of those tokens in shared memory (fp64 trig, rounded once to bf16),
 // then half-warps walk the (token, head) rows: 16 lanes x 16 bytes = one
 // 128-dim head row, so every global access is a coalesced 16-byte vector.
@@ -21,8 +21,8 @@
 namespace vj {
 namespace {
 
-constexpr int kTokPerCta = 8;
-constexpr int kThreads = 256;
+constexpr int kTokPerCta = 2;   // small CTAs: a decode batch of 512 tokens still fills the GPU
+constexpr int kThreads = 128;
 constexpr int kHeadDim = 128;
 constexpr int kPairs = kHeadDim / 2;
 

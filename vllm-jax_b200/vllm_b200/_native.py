@@ -54,6 +54,8 @@ PROTOTYPES: dict[str, tuple] = {
         c_i32, c_i32, c_i32, c_i32, c_i32,          # block_size, width, bucket_tokens, bucket_batch, flags
         c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,         # ids, positions, slots, block_tables, cu, ctx
         c_vp, c_vp]),                               # error_flag, stream
+    "vj_add_rmsnorm": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_f32, c_vp]),
+    "vj_silu_mul": (c_int, [c_vp, c_vp, c_i64, c_i32, c_vp]),
     "vj_scatter_rows": (c_int, [c_vp, c_vp, c_i32, c_vp, c_i32, c_i32, c_vp, c_vp, c_vp]),
     "vj_argmax_append": (c_int, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_i32, c_vp, c_vp,
                                  c_vp]),

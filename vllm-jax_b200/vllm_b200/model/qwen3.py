@@ -27,6 +27,7 @@ import torch
 import torch.nn.functional as F
 
 from ..kernels.decode_paged_attention import paged_decode
+from ..kernels.fused import add_rmsnorm, silu_mul
 from ..kernels.kv_store import kv_store_qknorm_rope, update_kv_cache
 from ..kernels.prefill_paged_attention import paged_prefill
 
@@ -203,11 +204,14 @@ class Qwen3Model:
             torch.distributed.all_reduce(x, group=self.pg)
         return x
 
-    def _layer(self, l: int, x: torch.Tensor, kv_cache: torch.Tensor, meta, attn_fn):
+    def _layer(self, l: int, x: torch.Tensor, h: torch.Tensor, kv_cache: torch.Tensor, meta,
+               attn_fn):
+        """x: residual stream entering layer l; h = input_layernorm(x). Returns
+        (x + attn, post-attention-normed) -> MLP output d; the caller fuses
+        x + d with the next norm."""
         lw = self.w.layers[l]
         c = self.cfg
         T = x.shape[0]
-        h = rms_norm(x, lw.ln1, c.rms_norm_eps)
         qkv = F.linear(h, lw.w_qkv)
         q, k, v = torch.split(qkv, [self.hq * self.d, self.hkv * self.d, self.hkv * self.d], -1)
         q = kv_store_qknorm_rope(q.view(T, self.hq, self.d), k.view(T, self.hkv, self.d),
@@ -216,13 +220,20 @@ class Qwen3Model:
                                  eps=c.rms_norm_eps, rope_theta=c.rope_theta)
         o = attn_fn(q, kv_cache).reshape(T, self.hq * self.d)
         o = self._all_reduce(F.linear(o, lw.w_o))
-        x = x + o                                   # attn_output += x (bf16)
-        h = rms_norm(x, lw.ln2, c.rms_norm_eps)
-        gu = F.linear(h, lw.w_gate_up)
-        g, u = gu.chunk(2, dim=-1)
-        m = F.silu(g) * u
+        x, h = add_rmsnorm(o, lw.ln2, c.rms_norm_eps, residual=x)   # attn_output += x; norm
+        m = silu_mul(F.linear(h, lw.w_gate_up))
         d = self._all_reduce(F.linear(m, lw.w_down))
-        return x + d
+        return x, d
+
+    def _stack(self, x: torch.Tensor, kv_caches, meta, attn_fn) -> torch.Tensor:
+        c = self.cfg
+        L = c.num_hidden_layers
+        h = add_rmsnorm(x, self.w.layers[0].ln1, c.rms_norm_eps)
+        for l in range(L):
+            x, d = self._layer(l, x, h, kv_caches[l], meta, attn_fn)
+            w_next = self.w.layers[l + 1].ln1 if l + 1 < L else self.w.norm
+            x, h = add_rmsnorm(d, w_next, c.rms_norm_eps, residual=x)  # outputs = residual + mlp
+        return h    # final norm applied
 
     def embed(self, input_ids: torch.Tensor) -> torch.Tensor:
         return F.embedding(input_ids.long(), self.w.embed)
@@ -239,9 +250,7 @@ class Qwen3Model:
                                  getattr(meta, "context_lens", None),
                                  max_seqlen_q=meta.max_seqlen_bucket, scale=self.scale)
 
-        for l in range(self.cfg.num_hidden_layers):
-            x = self._layer(l, x, kv_caches[l], meta, attn)
-        return rms_norm(x, self.w.norm, self.cfg.rms_norm_eps)
+        return self._stack(x, kv_caches, meta, attn)
 
     def forward_decode(self, meta, kv_caches: list[torch.Tensor]) -> torch.Tensor:
         """One token per row; returns bf16 logits [rows, vocab]."""
@@ -250,7 +259,5 @@ class Qwen3Model:
         def attn(q, kv):
             return paged_decode(q, kv, meta.block_tables, meta.context_lens, self.scale)
 
-        for l in range(self.cfg.num_hidden_layers):
-            x = self._layer(l, x, kv_caches[l], meta, attn)
-        x = rms_norm(x, self.w.norm, self.cfg.rms_norm_eps)
+        x = self._stack(x, kv_caches, meta, attn)
         return F.linear(x, self.w.lm_head)           # compute_logits (qwen3.py:474-477)
