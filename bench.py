@@ -610,12 +610,19 @@ def run_e2e(args, rank, world, local_rank):
                    tensor_parallel_size=world, gpu_memory_utilization=0.9,
                    max_model_len=((max_len + 15) // 16) * 16, compat=False)
     pg = dist.group.WORLD if world > 1 else None
+
+    def progress(msg):
+        print(f"[rank {rank}] {msg}", file=sys.stderr, flush=True)
+
     eng = Engine(econf, dev, seed=0, process_group=pg, max_slots=cfg["num_requests"] + 8)
+    progress(f"engine ready ({eng.config.num_blocks} blocks)")
     eng.runner.capture_all(cfg["max_num_seqs"])
+    progress("decode graphs captured" if eng.runner.use_cuda_graphs else "eager decode (TP)")
     # warm-up: a few short requests (cuBLAS heuristics, prefill kernels)
     for _ in range(max(args.warmup, 1)):
         eng.generate(prompts[:8], SamplingParams(temperature=0, max_new_tokens=4,
                                                  ignore_eos=True))
+    progress("warm-up done")
     params = [SamplingParams(temperature=0, max_new_tokens=o, ignore_eos=True) for o in outs]
     times, stats = [], []
     launches0 = _native.launch_count
@@ -632,6 +639,7 @@ def run_e2e(args, rank, world, local_rank):
             t1 = time.perf_counter()
         times.append(t1 - t0)
         stats.append(dict(eng.stats))
+        progress(f"timed generate: {t1 - t0:.2f} s")
         assert [len(r) for r in res] == outs
     t = torch.tensor([max(times)], dtype=torch.float64, device=dev)
     if world > 1:

@@ -51,7 +51,9 @@ class ModelRunner:
         self.tables = DeviceTables(max_slots, config.max_len, self.width, config.block_size,
                                    device)
         self.free_slots = list(range(max_slots - 1, -1, -1))
-        self.use_cuda_graphs = use_cuda_graphs
+        # Collectives of torch.distributed are not captured into CUDA graphs
+        # here: with tensor parallelism the decode step runs eagerly.
+        self.use_cuda_graphs = use_cuda_graphs and tp_size == 1
         self.graphs: dict[int, tuple[torch.cuda.CUDAGraph, DecodeMeta, torch.Tensor]] = {}
         self.graph_launches: dict[int, int] = {}
         self._tok_host = torch.empty(max(config.max_num_seqs, 1), dtype=torch.int32).pin_memory()
@@ -107,6 +109,8 @@ class ModelRunner:
         return self.graphs[bb]
 
     def capture_all(self, max_batch: int) -> None:
+        if not self.use_cuda_graphs:
+            return
         b = 1
         while True:
             self._decode_graph(b)
