@@ -208,7 +208,9 @@ VJ_API vj_status vj_silu_mul(const void *gate_up, void *out, int64_t rows,
  *   token_table [max_slots, token_stride]  token ids of each request
  *   block_pool  [max_slots, bt_stride]     its allocated block ids
  *   num_blocks  [max_slots]                number of valid entries
- * Per call: seq_slots[num_seqs], seq_lens[num_seqs] (= len(request)).
+ * Per call: seq_slots[num_seqs], seq_lens[num_seqs] (= len(request), or the
+ * number of new tokens in VJ_META_RANGES mode), seq_starts[num_seqs] (ranges
+ * mode only, else NULL: first new position, i.e. tokens already cached).
  * Prefill (mode VJ_META_PREFILL): all len tokens of each sequence, packed;
  *   input_ids/positions/slot_mapping [bucket_tokens] padded with 0/0/-1;
  *   cu_seqlens [bucket_batch + 1] padded by repeating the total;
@@ -222,12 +224,12 @@ VJ_API vj_status vj_silu_mul(const void *gate_up, void *out, int64_t rows,
  * error_flag (device int32) is set to 1 (position without an allocated
  * block), 2 (tokens exceed bucket_tokens) or 3 (bad scatter row).
  * ------------------------------------------------------------------------- */
-enum { VJ_META_PREFILL = 0, VJ_META_DECODE = 1 };
+enum { VJ_META_PREFILL = 0, VJ_META_DECODE = 1, VJ_META_RANGES = 2 };
 enum { VJ_META_LAST_BLOCK_SLOT = 1 };
 
 VJ_API vj_status vj_build_metadata(
-    int32_t mode, const int32_t *seq_slots, const int32_t *seq_lens,
-    int32_t num_seqs, const int32_t *token_table, int32_t token_stride,
+    int32_t mode, const int32_t *seq_slots, const int32_t *seq_starts,
+    const int32_t *seq_lens, int32_t num_seqs, const int32_t *token_table, int32_t token_stride,
     const int32_t *block_pool, const int32_t *num_blocks, int32_t bt_stride,
     int32_t block_size, int32_t width, int32_t bucket_tokens,
     int32_t bucket_batch, int32_t flags, int32_t *input_ids, int32_t *positions,

@@ -77,3 +77,32 @@ def prepare_decode(tokens: list[list[int]], blocks: list[list[int]], block_size:
             "slot_mapping": np.asarray(slots, np.int32),
             "block_tables": pad_block_tables(blocks, bucket, max_blocks_per_seq),
             "context_lens": np.asarray(ctx, np.int32)}
+
+
+def prepare_ranges(tokens: list[list[int]], blocks: list[list[int]], starts: list[int],
+                   ns: list[int], block_size: int, bucket_batch: int,
+                   max_blocks_per_seq: int) -> dict:
+    """Chunked-prefill packing (no counterpart in the reference, which always
+    prefills from position 0): sequence s contributes tokens [starts[s],
+    starts[s] + ns[s]) at those positions with position-addressed slots;
+    context_lens = start + n; padding like prepare_prefill (tokens to a power
+    of two with (0, 0, -1), cu_seqlens repeated, context_lens 0)."""
+    ids, pos, slots, cu = [], [], [], [0]
+    for tok, blk, a, n in zip(tokens, blocks, starts, ns):
+        for t in range(a, a + n):
+            ids.append(tok[t])
+            pos.append(t)
+            slots.append(blk[t // block_size] * block_size + t % block_size)
+        cu.append(cu[-1] + n)
+    total = len(ids)
+    pad = bucket_size(total) - total
+    ids += [0] * pad
+    pos += [0] * pad
+    slots += [-1] * pad
+    cu += [cu[-1]] * (bucket_batch + 1 - len(cu))
+    ctx = [a + n for a, n in zip(starts, ns)]
+    ctx += [0] * (bucket_batch - len(ctx))
+    return {"input_ids": np.asarray(ids, np.int32), "positions": np.asarray(pos, np.int32),
+            "slot_mapping": np.asarray(slots, np.int32),
+            "block_tables": pad_block_tables(blocks, bucket_batch, max_blocks_per_seq),
+            "cu_seqlens_q": np.asarray(cu, np.int32), "context_lens": np.asarray(ctx, np.int32)}

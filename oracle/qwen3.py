@@ -131,6 +131,85 @@ class OracleQwen3:
         return _mm(x, self.W["lm_head"])
 
 
+def _mixed_attn(model, starts, ns, tables):
+    """Attention of a chunked step: new token i of sequence s sits at position
+    starts[s] + i and attends to the cached keys [0, starts[s] + i] read
+    through its block table. One-token rows scale q like the reference's
+    decode (q / bf16(sqrt(D))), longer rows like its prefill (q * bf16(1/sqrt(D)))."""
+    c = model.cfg
+    D = c.head_dim
+    g = c.num_attention_heads // c.num_key_value_heads
+    sq = np.float32(bf16(np.float32(np.sqrt(np.float32(D)))))
+    qscale = np.float32(bf16(np.float32(1.0 / np.sqrt(D))))
+
+    def attn(l, q):
+        out = np.zeros_like(q)
+        a = 0
+        for s, (st, n) in enumerate(zip(starts, ns)):
+            L = st + n
+            k = gather_pages(model.kc[l], tables[s], L).transpose(1, 0, 2)   # [Hkv, L, D]
+            v = gather_pages(model.vc[l], tables[s], L).transpose(1, 0, 2)
+            qs = bf16(q[a:a + n] / sq) if n == 1 else bf16(q[a:a + n] * qscale)
+            qh = qs.reshape(n, -1, g, D).transpose(1, 2, 0, 3)               # [Hkv, g, n, D]
+            sc = np.matmul(qh, k[:, None].transpose(0, 1, 3, 2))             # [Hkv, g, n, L]
+            mask = (np.arange(L)[None, :] <= (st + np.arange(n))[:, None])[None, None]
+            o = _softmax_pv(sc, v[:, None], mask)
+            out[a:a + n] = bf16(o.transpose(2, 0, 1, 3).reshape(n, -1, D))
+            a += n
+        return out
+    return attn
+
+
+def mixed_step(model: OracleQwen3, ids, starts, ns, tables, sample_rows):
+    """One chunked-prefill forward (tokens packed in sequence order, no
+    padding); returns logits [len(sample_rows), vocab]."""
+    c, bs = model.cfg, model.bs
+    pos, slots = [], []
+    for st, n, tb in zip(starts, ns, tables):
+        for t in range(st, st + n):
+            pos.append(t)
+            slots.append(int(tb[t // bs]) * bs + t % bs)
+    attn = _mixed_attn(model, starts, ns, tables)
+    x = bf16(model.W["embed"][np.asarray(ids)])
+    for l in range(c.num_hidden_layers):
+        x = model._layer(l, x, pos, slots, attn)
+    x = okv.rmsnorm(x[np.asarray(sample_rows, np.int64)], model.W["norm"], c.rms_norm_eps)
+    return _mm(x, model.W["lm_head"])
+
+
+def greedy_replay_chunked(model: OracleQwen3, trace: list, prompts: list[list[int]],
+                          first_id: int = 0):
+    """Replay a recorded chunked schedule (per step: (request id, start, n)
+    and each request's block ids) with the oracle's own tokens. Returns
+    (tokens per request index, per step a dict request index -> (top id, top
+    logit, top-2 gap))."""
+    tokens = {i: list(p) for i, p in enumerate(prompts)}
+    gaps = []
+    for st in trace:
+        rows = [(rid - first_id, a, n) for rid, a, n in st["batch"]]
+        ids, starts, ns, tables, sample, picked = [], [], [], [], [], []
+        off = 0
+        for (r, a, n), (rid, _, _) in zip(rows, st["batch"]):
+            ids.extend(tokens[r][a:a + n])
+            starts.append(a)
+            ns.append(n)
+            tables.append(np.asarray(st["blocks"][rid]))
+            off += n
+            if a + n == len(tokens[r]):
+                sample.append(off - 1)
+                picked.append(r)
+        logits = mixed_step(model, ids, starts, ns, tables, sample)
+        step = {}
+        for row, r in enumerate(picked):
+            lg = logits[row]
+            top = int(np.argmax(lg))
+            srt = np.sort(lg)
+            step[r] = (top, float(srt[-1]), float(srt[-1] - srt[-2]))
+            tokens[r].append(top)
+        gaps.append(step)
+    return tokens, gaps
+
+
 def greedy_replay(model: OracleQwen3, trace: dict, prompts: list[list[int]]):
     """Replay the scheduled steps of a golden host trace (block tables, slots
     and positions depend only on lengths there) with the oracle's own tokens.

@@ -25,8 +25,9 @@ constexpr int kMetaThreads = 512;
 constexpr int kMaxSeqsScan = 8192;   // sequences per step handled by the in-CTA scan
 
 struct MetaArgs {
-  int mode;  // VJ_META_PREFILL / VJ_META_DECODE
+  int mode;  // VJ_META_PREFILL / VJ_META_DECODE / VJ_META_RANGES
   const int32_t *seq_slots, *seq_lens;
+  const int32_t *seq_starts;  // VJ_META_RANGES: first new position of each sequence
   int num_seqs;
   const int32_t *token_table;
   int token_stride;
@@ -51,7 +52,7 @@ build_metadata_kernel(MetaArgs a) {
   const int tid = threadIdx.x;
   const int S = a.num_seqs;
 
-  if (a.mode == VJ_META_PREFILL) {
+  if (a.mode == VJ_META_PREFILL || a.mode == VJ_META_RANGES) {
     // ---- cu_seqlens: exclusive scan of the lengths (every CTA redoes it; S is small)
     const int per = (S + kMetaThreads - 1) / kMetaThreads;
     const int b0 = tid * per;
@@ -99,7 +100,7 @@ build_metadata_kernel(MetaArgs a) {
           if (cu[mid] <= t) lo = mid; else hi = mid - 1;
         }
         const int slot = __ldg(a.seq_slots + lo);
-        pos = t - cu[lo];
+        pos = t - cu[lo] + (a.mode == VJ_META_RANGES ? __ldg(a.seq_starts + lo) : 0);
         id = __ldg(a.token_table + (size_t)slot * a.token_stride + pos);
         sl = slot_of(a, slot, pos);
         if (sl < 0) atomicExch(a.error_flag, 1);
@@ -111,6 +112,12 @@ build_metadata_kernel(MetaArgs a) {
     // ---- cu_seqlens padded to bucket_batch + 1 by repeating the total
     for (int s = gtid; s <= a.bucket_batch; s += gstride) {
       a.cu_seqlens[s] = s <= S ? cu[s] : total;
+    }
+    // ---- ranges: keys per sequence = start + new tokens (0 for padding rows)
+    if (a.mode == VJ_META_RANGES && a.context_lens) {
+      for (int s = gtid; s < a.bucket_batch; s += gstride) {
+        a.context_lens[s] = s < S ? __ldg(a.seq_starts + s) + __ldg(a.seq_lens + s) : 0;
+      }
     }
   } else {
     // ---- decode: one row per scheduled sequence, padding (0, 0, ctx 0, slot -1)
@@ -230,15 +237,20 @@ argmax_append_kernel(const __nv_bfloat16 *__restrict__ logits, int64_t row_strid
 }  // namespace vj
 
 extern "C" vj_status vj_build_metadata(
-    int32_t mode, const int32_t *seq_slots, const int32_t *seq_lens, int32_t num_seqs,
+    int32_t mode, const int32_t *seq_slots, const int32_t *seq_starts, const int32_t *seq_lens,
+    int32_t num_seqs,
     const int32_t *token_table, int32_t token_stride, const int32_t *block_pool,
     const int32_t *num_blocks, int32_t bt_stride, int32_t block_size, int32_t width,
     int32_t bucket_tokens, int32_t bucket_batch, int32_t flags, int32_t *input_ids,
     int32_t *positions, int32_t *slot_mapping, int32_t *block_tables, int32_t *cu_seqlens,
     int32_t *context_lens, int32_t *error_flag, cudaStream_t stream) {
   using namespace vj;
-  if (mode != VJ_META_PREFILL && mode != VJ_META_DECODE) {
-    return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_build_metadata: mode must be prefill or decode");
+  if (mode != VJ_META_PREFILL && mode != VJ_META_DECODE && mode != VJ_META_RANGES) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT,
+                     "vj_build_metadata: mode must be prefill, decode or ranges");
+  }
+  if (mode == VJ_META_RANGES && !seq_starts) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_build_metadata: ranges need seq_starts");
   }
   if (num_seqs < 0 || token_stride <= 0 || bt_stride < width || block_size <= 0 || width < 0 ||
       bucket_tokens < 0 || bucket_batch < 0) {
@@ -247,17 +259,18 @@ extern "C" vj_status vj_build_metadata(
   if (mode == VJ_META_DECODE && bucket_tokens < num_seqs) {
     return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_build_metadata: decode bucket smaller than batch");
   }
-  if (mode == VJ_META_PREFILL && (bucket_batch < num_seqs || num_seqs > kMaxSeqsScan)) {
+  if (mode != VJ_META_DECODE && (bucket_batch < num_seqs || num_seqs > kMaxSeqsScan)) {
     return set_error(VJ_ERR_INVALID_ARGUMENT,
                      "vj_build_metadata: prefill needs num_seqs <= bucket_batch and <= 8192");
   }
   if (!seq_slots || !seq_lens || !token_table || !block_pool || !num_blocks || !input_ids ||
       !positions || !slot_mapping || !block_tables || !error_flag ||
-      (mode == VJ_META_PREFILL && !cu_seqlens)) {
+      (mode != VJ_META_DECODE && !cu_seqlens)) {
     return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_build_metadata: null pointer");
   }
   MetaArgs a;
-  a.mode = mode; a.seq_slots = seq_slots; a.seq_lens = seq_lens; a.num_seqs = num_seqs;
+  a.mode = mode; a.seq_slots = seq_slots; a.seq_starts = seq_starts; a.seq_lens = seq_lens;
+  a.num_seqs = num_seqs;
   a.token_table = token_table; a.token_stride = token_stride;
   a.block_pool = block_pool; a.num_blocks = num_blocks;
   a.bt_stride = bt_stride; a.block_size = block_size; a.width = width;

@@ -49,7 +49,7 @@ PROTOTYPES: dict[str, tuple] = {
         c_i64, c_i64, c_i64,                        # strides
         c_i32, c_f32, c_vp, c_vp]),                 # max_seqlen_q, scale, err, stream
     "vj_build_metadata": (c_int, [
-        c_i32, c_vp, c_vp, c_i32,                   # mode, seq_slots, seq_lens, num_seqs
+        c_i32, c_vp, c_vp, c_vp, c_i32,             # mode, slots, starts, lens, num_seqs
         c_vp, c_i32, c_vp, c_vp, c_i32,             # token_table, stride, block_pool, nblocks, bt_stride
         c_i32, c_i32, c_i32, c_i32, c_i32,          # block_size, width, bucket_tokens, bucket_batch, flags
         c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,         # ids, positions, slots, block_tables, cu, ctx
@@ -64,7 +64,7 @@ PROTOTYPES: dict[str, tuple] = {
 # vj_status codes (include/vjattn.h)
 VJ_OK, VJ_ERR_INVALID_ARGUMENT, VJ_ERR_UNSUPPORTED, VJ_ERR_WORKSPACE, VJ_ERR_CUDA = range(5)
 VJ_KV_NORM, VJ_KV_ROPE, VJ_KV_WRAP_NEGATIVE = 1, 2, 4
-VJ_META_PREFILL, VJ_META_DECODE = 0, 1
+VJ_META_PREFILL, VJ_META_DECODE, VJ_META_RANGES = 0, 1, 2
 VJ_META_LAST_BLOCK_SLOT = 1
 
 

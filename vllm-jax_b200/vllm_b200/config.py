@@ -19,6 +19,10 @@ class Config:
     # finished requests keep their blocks (scheduler.py:65-70) and a decode
     # token is stored in the last allocated block (model_runner.py:282-284).
     compat: bool = True
+    # Token-budget scheduling with prompts split into chunks that share a
+    # forward with decode rows (not in the reference). Implies compat=False
+    # behaviour: position-addressed slots and blocks freed on finish.
+    enable_chunked_prefill: bool = False
 
     @property
     def max_len(self) -> int:

@@ -47,6 +47,23 @@ class DecodeMeta:
     num_seqs: int
 
 
+@dataclass
+class RangesMeta:
+    """Mixed batch: sequence s contributes positions [start_s, start_s + n_s)."""
+    input_ids: torch.Tensor
+    positions: torch.Tensor
+    slot_mapping: torch.Tensor
+    block_tables: torch.Tensor     # [bucket_batch, width]
+    cu_seqlens_q: torch.Tensor     # [bucket_batch + 1]
+    context_lens: torch.Tensor     # [bucket_batch] keys per sequence (start + n)
+    num_seqs: int
+    num_tokens: int
+    max_new: int
+    sample_rows: torch.Tensor      # packed row of each sampled sequence's last token
+    sample_slots: torch.Tensor     # their token-table rows
+    sample_lens: torch.Tensor      # and lengths (the sampled token is stored there)
+
+
 class DeviceTables:
     """Token and block tables of every live request slot, kept on the GPU."""
 
@@ -124,7 +141,7 @@ class DeviceTables:
         sm = torch.empty_like(ids)
         tables = torch.empty((max_num_seqs, width), dtype=torch.int32, device=dev)
         cu = torch.empty(max_num_seqs + 1, dtype=torch.int32, device=dev)
-        _native.call("vj_build_metadata", _native.VJ_META_PREFILL, d_slots.data_ptr(),
+        _native.call("vj_build_metadata", _native.VJ_META_PREFILL, d_slots.data_ptr(), None,
                      d_lens.data_ptr(), S, self.tokens.data_ptr(), self.tokens.stride(0),
                      self.blocks.data_ptr(), self.num_blocks.data_ptr(), self.blocks.stride(0),
                      self.block_size, width, bt, max_num_seqs, 0, ids.data_ptr(),
@@ -132,6 +149,43 @@ class DeviceTables:
                      self.error.data_ptr(), stream_ptr(dev))
         return PrefillMeta(ids, pos, sm, tables, cu, max(lens), bucket_size(max(lens)),
                            d_lens.clone(), S, total)
+
+    def build_ranges(self, slots: list[int], starts: list[int], ns: list[int], width: int,
+                     sample: list[int], bucket_batch: int | None = None) -> RangesMeta:
+        """Metadata of a mixed batch (chunked prefill + decode) with vj_build_metadata
+        in ranges mode: sequence s contributes positions [starts[s], starts[s] +
+        ns[s]); tokens are padded to a power of two like prefill. `sample` lists
+        the sequences whose last row is sampled. One host->device upload."""
+        S = len(slots)
+        total = int(sum(ns))
+        bt = bucket_size(total)
+        bb = bucket_batch or S
+        ends = np.cumsum(np.asarray(ns, np.int64))
+        sample = np.asarray(sample, np.int64)
+        arr = self._upload(np.concatenate([
+            np.asarray(slots, np.int32), np.asarray(starts, np.int32),
+            np.asarray(ns, np.int32), (ends[sample] - 1).astype(np.int32),
+            np.asarray(slots, np.int32)[sample],
+            (np.asarray(starts, np.int64) + np.asarray(ns, np.int64))[sample].astype(np.int32)]))
+        d_slots, d_starts, d_ns = arr[:S], arr[S:2 * S], arr[2 * S:3 * S]
+        K = sample.size
+        rows = arr[3 * S:3 * S + K]
+        s_slots, s_lens = arr[3 * S + K:3 * S + 2 * K], arr[3 * S + 2 * K:3 * S + 3 * K]
+        dev = self.device
+        ids = torch.empty(bt, dtype=torch.int32, device=dev)
+        pos = torch.empty_like(ids)
+        sm = torch.empty_like(ids)
+        tables = torch.empty((bb, width), dtype=torch.int32, device=dev)
+        cu = torch.empty(bb + 1, dtype=torch.int32, device=dev)
+        ctx = torch.empty(bb, dtype=torch.int32, device=dev)
+        _native.call("vj_build_metadata", _native.VJ_META_RANGES, d_slots.data_ptr(),
+                     d_starts.data_ptr(), d_ns.data_ptr(), S, self.tokens.data_ptr(),
+                     self.tokens.stride(0), self.blocks.data_ptr(), self.num_blocks.data_ptr(),
+                     self.blocks.stride(0), self.block_size, width, bt, bb, 0, ids.data_ptr(),
+                     pos.data_ptr(), sm.data_ptr(), tables.data_ptr(), cu.data_ptr(),
+                     ctx.data_ptr(), self.error.data_ptr(), stream_ptr(dev))
+        return RangesMeta(ids, pos, sm, tables, cu, ctx, S, total, max(ns), rows,
+                          s_slots, s_lens)
 
     def build_decode(self, slots: list[int], lens: list[int], width: int,
                      last_block_slot: bool = True, out: DecodeMeta | None = None) -> DecodeMeta:
@@ -152,7 +206,7 @@ class DeviceTables:
             sm = torch.empty_like(ids)
             ctx = torch.empty_like(ids)
             tables = torch.empty((bb, width), dtype=torch.int32, device=dev)
-        _native.call("vj_build_metadata", _native.VJ_META_DECODE, d_slots.data_ptr(),
+        _native.call("vj_build_metadata", _native.VJ_META_DECODE, d_slots.data_ptr(), None,
                      d_lens.data_ptr(), B, self.tokens.data_ptr(), self.tokens.stride(0),
                      self.blocks.data_ptr(), self.num_blocks.data_ptr(), self.blocks.stride(0),
                      self.block_size, width, bb, bb,

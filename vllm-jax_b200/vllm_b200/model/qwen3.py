@@ -261,3 +261,26 @@ class Qwen3Model:
 
         x = self._stack(x, kv_caches, meta, attn)
         return F.linear(x, self.w.lm_head)           # compute_logits (qwen3.py:474-477)
+
+    def forward_mixed(self, meta, kv_caches: list[torch.Tensor], num_decode: int,
+                      sample_rows: torch.Tensor) -> torch.Tensor:
+        """Chunked-prefill step over meta (ranges metadata): sequences
+        [0, num_decode) contribute one token each and go through the decode
+        kernel; the rest are prompt chunks after a cached prefix (prefill
+        kernel with context_lens). Returns bf16 logits of `sample_rows`."""
+        x = self.embed(meta.input_ids)
+        S, nd = meta.num_seqs, num_decode
+
+        def attn(q, kv):
+            out = torch.empty_like(q)
+            if nd:
+                paged_decode(q[:nd], kv, meta.block_tables[:nd], meta.context_lens[:nd],
+                             self.scale, out=out[:nd])
+            if S > nd:
+                paged_prefill(q, kv, meta.block_tables[nd:S], meta.cu_seqlens_q[nd:S + 1],
+                              meta.context_lens[nd:S], max_seqlen_q=meta.max_new,
+                              scale=self.scale, out=out)
+            return out
+
+        x = self._stack(x, kv_caches, meta, attn)
+        return F.linear(x.index_select(0, sample_rows), self.w.lm_head)

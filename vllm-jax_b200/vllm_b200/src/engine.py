@@ -27,7 +27,7 @@ from ..sampling_params import SamplingParams
 from .kv_cache_manager import KVCacheManager
 from .model_runner import ModelRunner, kv_cache_bytes_per_block
 from .request import Request
-from .scheduler import Scheduler
+from .scheduler import ChunkedScheduler, Scheduler
 
 
 class Engine:
@@ -68,8 +68,15 @@ class Engine:
                                              group=process_group)
                 num_blocks = int(t.item())
             self.config = config = dataclasses.replace(config, num_blocks=num_blocks)
+        if config.enable_chunked_prefill:
+            if config.compat:
+                self.config = config = dataclasses.replace(config, compat=False)
+            if num_blocks < config.max_blocks_per_seq:
+                raise ValueError("chunked prefill needs a pool of at least max_model_len tokens")
         self.kv = KVCacheManager(num_blocks, config.block_size)
-        self.scheduler = Scheduler(config, self.kv)
+        self.scheduler = (ChunkedScheduler(config, self.kv) if config.enable_chunked_prefill
+                          else Scheduler(config, self.kv))
+        self.trace: list | None = None     # set to a list to record chunked steps
         self.runner = ModelRunner(config, self.mcfg, self.kv, device, tp_rank=self.tp_rank,
                                   tp_size=self.tp_size, process_group=process_group,
                                   weights=self.weights, max_slots=max_slots,
@@ -97,6 +104,8 @@ class Engine:
 
     # ---------------------------------------------------------------- loop
     def step(self) -> list[tuple[int, int]]:
+        if self.config.enable_chunked_prefill:
+            return self._step_chunked()
         decode, prefill = self.scheduler.schedule()
         st = self.stats
         st["decode_ctx_tokens"] += sum(len(r) for r in decode)
@@ -108,6 +117,29 @@ class Engine:
         st["prefill_tokens"] += sum(len(r) for r in prefill)
         done = []
         for r in decode:
+            if r.is_finished():
+                done.append((r.id, r.num_completion_tokens))
+                self.runner.release(r)
+                del self.live[r.id]
+        return done
+
+    def _step_chunked(self) -> list[tuple[int, int]]:
+        batch = self.scheduler.schedule()
+        if not batch:
+            raise RuntimeError("chunked scheduler made no progress (pool too small?)")
+        st = self.stats
+        if self.trace is not None:
+            self.trace.append({"batch": [(r.id, r.num_computed_tokens, n) for r, n in batch],
+                               "blocks": {r.id: self.kv.block_ids(r) for r, _ in batch}})
+        sampled = self.runner.run_chunked(batch, self.live, st)
+        self.scheduler.postprocess(batch, sampled)
+        st["steps"] += 1
+        st["decode_tokens"] += len(sampled)
+        st["decode_steps"] += 1
+        st["prefill_tokens"] += sum(n for r, n in batch if n > 1 or r.id not in sampled)
+        st["decode_ctx_tokens"] += sum(r.num_computed_tokens for r, _ in batch)
+        done = []
+        for r, _ in batch:
             if r.is_finished():
                 done.append((r.id, r.num_completion_tokens))
                 self.runner.release(r)

@@ -69,6 +69,20 @@ class KVCacheManager:
             self._take(table)
             self.dirty.add(request.id)
 
+    # -- token-budget (chunked prefill) mode, beyond the reference ----------
+    def can_grow(self, request: Request, total_tokens: int) -> bool:
+        need = ceil_div(total_tokens, self.block_size) - len(self.get_block_table(request))
+        return need <= len(self.free_block_queue)
+
+    def grow(self, request: Request, total_tokens: int) -> None:
+        """Own enough blocks for positions [0, total_tokens)."""
+        table = self.get_block_table(request)
+        need = ceil_div(total_tokens, self.block_size)
+        if len(table) < need:
+            while len(table) < need:
+                self._take(table)
+            self.dirty.add(request.id)
+
     def deallocate(self, request: Request) -> None:
         table = self.get_block_table(request)
         for block in table:

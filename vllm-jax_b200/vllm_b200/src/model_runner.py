@@ -177,3 +177,59 @@ class ModelRunner:
                 torch.cuda.current_stream(self.device).synchronize()
                 stats["prefill_s"] += time.perf_counter() - t1
         return out
+
+    # ------------------------------------------------------------------ chunked step
+    def run_chunked(self, batch: list[tuple[Request, int]], live: dict[int, Request],
+                    stats: dict | None = None) -> dict[int, int]:
+        """One step of the token-budget scheduler: (request, n) computes
+        positions [num_computed_tokens, +n) of each request in ONE forward.
+        A request whose last known token is among them samples a token, which
+        is appended to it. Returns {request id: token}.
+
+        All-decode steps (every row one token and sampled) replay the decode
+        CUDA graph; mixed steps run eagerly with the decode kernel on the
+        one-token rows and the prefill kernel, with its cached prefix, on the
+        chunks."""
+        t0 = time.perf_counter()
+        for r, _ in batch:
+            if r.slot < 0 and stats is not None:
+                stats["h2d_bytes"] += 4 * len(r.token_ids)
+            self._assign_slot(r)
+        self._sync_blocks(live)
+        sampled = [r for r, n in batch if r.num_computed_tokens + n == len(r)]
+        if all(n == 1 for _, n in batch) and len(sampled) == len(batch):
+            toks = self.decode([r for r, _ in batch])
+            if stats is not None:
+                stats["decode_s"] += time.perf_counter() - t0
+                stats["h2d_bytes"] += 8 * len(batch)
+                stats["d2h_bytes"] += 4 * len(batch)
+        else:
+            order = sorted(range(len(batch)), key=lambda i: batch[i][1] != 1)   # stable
+            rows = [batch[i] for i in order]
+            nd = sum(1 for _, n in rows if n == 1)
+            pick = [i for i, (r, n) in enumerate(rows) if r.num_computed_tokens + n == len(r)]
+            meta = self.tables.build_ranges([r.slot for r, _ in rows],
+                                            [r.num_computed_tokens for r, _ in rows],
+                                            [n for _, n in rows], self.width, pick)
+            logits = self.model.forward_mixed(meta, self.kv_caches, nd, meta.sample_rows)
+            K = len(pick)
+            toks = []
+            if K:
+                d = self.tables.argmax_append(logits, meta.sample_slots, meta.sample_lens)
+                host = self._tok_host if K <= self._tok_host.numel() else torch.empty(
+                    K, dtype=torch.int32).pin_memory()
+                host[:K].copy_(d, non_blocking=True)
+                torch.cuda.current_stream(self.device).synchronize()
+                toks = host[:K].tolist()
+            sampled = [rows[i][0] for i in pick]
+            if stats is not None:
+                torch.cuda.current_stream(self.device).synchronize()
+                stats["prefill_s"] += time.perf_counter() - t0
+                stats["h2d_bytes"] += 4 * (3 * len(rows) + 3 * K)
+                stats["d2h_bytes"] += 4 * K
+        out = {}
+        for r, t in zip(sampled, toks):
+            r.token_ids.append(t)
+            r.num_completion_tokens += 1
+            out[r.id] = t
+        return out

@@ -33,6 +33,7 @@ class Request:
         self.num_prompt_tokens = len(token_ids)
         self.num_completion_tokens = 0
         self.slot = -1
+        self.num_computed_tokens = 0   # chunked mode: positions whose KV is cached
 
     def is_finished(self) -> bool:
         return self.status == Status.FINISHED

@@ -84,3 +84,93 @@ class Scheduler:
                 self.finished_requests.append(request)
                 if not self.compat:
                     self.kv_cache_manager.deallocate(request)
+
+
+class ChunkedScheduler:
+    """Token-budget scheduler with chunked prefill mixed into decode steps.
+
+    Beyond the reference (whose prefill must fit the budget whole and runs in
+    a separate pass from decode, so a prompt >= max_num_batched_tokens is never
+    admitted): every step spends at most max_num_batched_tokens tokens over at
+    most max_num_seqs requests. Running requests come first, in order: one
+    token for a request whose known tokens are all cached (decode), else the
+    next chunk of its prompt; then waiting requests start their prompt with
+    whatever budget is left. A request samples a token when a step processes
+    its last known token. When the pool runs dry the request at the tail of
+    `running` is preempted (blocks freed, recomputed from scratch later) unless
+    a shorter chunk still fits. Finished requests always release their blocks."""
+
+    def __init__(self, config: Config, kv_cache_manager: KVCacheManager):
+        self.max_num_batched_tokens = config.max_num_batched_tokens
+        self.max_num_seqs = config.max_num_seqs
+        self.kv_cache_manager = kv_cache_manager
+        self.waiting: deque[Request] = deque()
+        self.running: deque[Request] = deque()
+        self.finished_requests: list[Request] = []
+
+    def is_finished(self) -> bool:
+        return not self.waiting and not self.running
+
+    def add(self, request: Request) -> None:
+        self.waiting.append(request)
+
+    def _preempt(self, request: Request) -> None:
+        request.status = Status.WAITING
+        request.num_computed_tokens = 0
+        self.running.remove(request)
+        self.waiting.appendleft(request)
+        self.kv_cache_manager.deallocate(request)
+
+    def schedule(self) -> list[tuple[Request, int]]:
+        """Returns (request, number of new tokens) in batch order."""
+        kv = self.kv_cache_manager
+        budget = self.max_num_batched_tokens
+        out: list[tuple[Request, int]] = []
+        i = 0
+        while i < len(self.running) and len(out) < self.max_num_seqs and budget > 0:
+            req = self.running[i]
+            n = min(len(req) - req.num_computed_tokens, budget)
+            while not kv.can_grow(req, req.num_computed_tokens + n):
+                # a shorter chunk that fits beats a preemption
+                fit = ((len(kv.get_block_table(req)) + len(kv.free_block_queue)) * kv.block_size
+                       - req.num_computed_tokens)
+                if fit >= 1:
+                    n = fit
+                    break
+                victim = self.running[-1]
+                self._preempt(victim)
+                if victim is req:
+                    n = 0
+                    break
+            if n <= 0:
+                break
+            kv.grow(req, req.num_computed_tokens + n)
+            out.append((req, n))
+            budget -= n
+            i += 1
+        while self.waiting and len(out) < self.max_num_seqs and budget > 0:
+            req = self.waiting[0]
+            n = min(len(req), budget)
+            if not kv.can_grow(req, n):
+                break
+            self.waiting.popleft()
+            req.status = Status.RUNNING
+            self.running.append(req)
+            kv.grow(req, n)
+            out.append((req, n))
+            budget -= n
+        return out
+
+    def postprocess(self, batch: list[tuple[Request, int]], sampled: dict[int, int]) -> None:
+        """Advance computed tokens; finish requests whose sampled token ends them."""
+        for req, n in batch:
+            req.num_computed_tokens += n
+            if req.id not in sampled:
+                continue
+            token = sampled[req.id]
+            if ((not req.ignore_eos and token == req.eos_token_id)
+                    or req.num_completion_tokens == req.max_new_tokens):
+                req.status = Status.FINISHED
+                self.running.remove(req)
+                self.finished_requests.append(req)
+                self.kv_cache_manager.deallocate(req)
