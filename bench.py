@@ -8,12 +8,17 @@ decode HBM GB/s (algorithmic bytes / time). One "step" = one decode-attention
 call over the whole batch (all KV heads of all sequences).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|prefill]
+                    [--workload decode|prefill|e2e|c5]
 
 N > 1 (torchrun, one process per GPU): tensor parallel by KV head -- rank r
 owns KV heads [r*8/N, (r+1)*8/N) of the same batch (its own pool slice); no
 collective on the data path. Total work is fixed, so scaling is "strong";
 `value` = algorithmic bytes of all ranks / max-over-ranks device time.
+
+--workload prefill: C2 paged prefill attention (TFLOP/s). --workload e2e: C4,
+Qwen3-8B continuous batching through Engine.generate (output tok/s).
+--workload c5: C5, Qwen3-32B with chunked prefill mixed with decode (output
+tok/s; --batch R runs the first R of the 1024 requests, and says so).
 
 --impl reference times the reference algorithm on the host CPU cores: the
 reference (JAX/Pallas) cannot be installed in this image, so its NumPy
@@ -572,6 +577,24 @@ C4 = dict(model="Qwen3-8B", num_requests=512, prompt_min=100, prompt_max=1024, o
           out_max=1024, max_num_batched_tokens=16384, max_num_seqs=512, seed=0)
 
 
+# C5: Qwen3-32B, chunked prefill mixed with decode.
+# Prompt lengths clip(lognormal(ln 1024, sigma), 32, 16384) with sigma = 1.0;
+# the token budget per step is not named by the config: 8192 is used.
+C5 = dict(model="Qwen3-32B", num_requests=1024, prompt_median=1024, sigma=1.0, prompt_min=32,
+          prompt_max=16384, out_min=64, out_max=2048, max_num_batched_tokens=8192,
+          max_num_seqs=512, seed=0)
+
+
+def c5_requests(cfg=C5, vocab=151936):
+    rng = np.random.default_rng(cfg["seed"])
+    n = cfg["num_requests"]
+    plen = np.clip(np.rint(rng.lognormal(math.log(cfg["prompt_median"]), cfg["sigma"], n)),
+                   cfg["prompt_min"], cfg["prompt_max"]).astype(np.int64)
+    olen = rng.integers(cfg["out_min"], cfg["out_max"] + 1, n)
+    prompts = [rng.integers(0, vocab, int(L)).tolist() for L in plen]
+    return prompts, [int(x) for x in olen]
+
+
 def c4_requests(cfg=C4, vocab=151936):
     rng = np.random.default_rng(cfg["seed"])
     n = cfg["num_requests"]
@@ -593,7 +616,8 @@ def run_e2e(args, rank, world, local_rank):
     from vllm_b200.model.qwen3 import get_config
     from vllm_b200.src.engine import Engine
 
-    cfg = dict(C4)
+    c5 = args.workload == "c5"
+    cfg = dict(C5 if c5 else C4)
     if args.model:
         cfg["model"] = args.model
     if args.batch is not None:
@@ -603,12 +627,13 @@ def run_e2e(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     mcfg = get_config(cfg["model"])
-    prompts, outs = c4_requests(cfg, mcfg.vocab_size)
+    prompts, outs = (c5_requests if c5 else c4_requests)(cfg, mcfg.vocab_size)
     max_len = max(len(p) + o for p, o in zip(prompts, outs))
     econf = Config(model=cfg["model"], max_num_batched_tokens=cfg["max_num_batched_tokens"],
                    max_num_seqs=cfg["max_num_seqs"], num_blocks=0, block_size=16,
                    tensor_parallel_size=world, gpu_memory_utilization=0.9,
-                   max_model_len=((max_len + 15) // 16) * 16, compat=False)
+                   max_model_len=((max_len + 15) // 16) * 16, compat=False,
+                   enable_chunked_prefill=c5)
     pg = dist.group.WORLD if world > 1 else None
 
     def progress(msg):
@@ -656,15 +681,25 @@ def run_e2e(args, rank, world, local_rank):
     kvb = mcfg.num_hidden_layers * 2 * (mcfg.num_key_value_heads // world) * mcfg.head_dim * 2
     dec_bytes = st["decode_steps"] * wbytes + st["decode_ctx_tokens"] * kvb
     achieved = dec_bytes / max(st["decode_s"], 1e-9) / 1e9
+    if c5:
+        metric = (f"output tok/s {cfg['model']} continuous batching with chunked prefill (C5: "
+                  f"{cfg['num_requests']} requests, prompts clip(lognormal(ln 1024, "
+                  f"{cfg['sigma']}), 32, 16384), outputs U[64,2048])")
+        workload = "C5 end-to-end, chunked prefill mixed with decode"
+    else:
+        metric = (f"output tok/s {cfg['model']} continuous batching (C4: "
+                  f"{cfg['num_requests']} requests, prompts U[100,1024], outputs U[100,1024])")
+        workload = "C4 end-to-end continuous batching"
     line = {
-        "metric": f"output tok/s {cfg['model']} continuous batching (C4: "
-                  f"{cfg['num_requests']} requests, prompts U[100,1024], outputs U[100,1024])",
+        "metric": metric,
         "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 1), "ms_per_step": round(wall * 1e3, 1),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded random token ids and lengths; random-init N(0,0.02) weights)",
-        "config": {"workload": "C4 end-to-end continuous batching", "model": cfg["model"],
+        "config": {"workload": workload, "model": cfg["model"],
                    "num_requests": cfg["num_requests"], "output_tokens": sum(outs),
+                   "prompt_tokens": sum(len(p) for p in prompts),
+                   "chunked_prefill": c5,
                    "max_num_batched_tokens": cfg["max_num_batched_tokens"],
                    "max_num_seqs": cfg["max_num_seqs"], "num_blocks": eng.config.num_blocks,
                    "parallelism": f"tp{world}" if world > 1 else "single GPU",
@@ -691,7 +726,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "prefill", "e2e"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "prefill", "e2e", "c5"], default="decode")
     ap.add_argument("--model", default=None, help="e2e: model preset (default Qwen3-8B)")
     ap.add_argument("--max-num-seqs", type=int, default=None, help="e2e: scheduler seats")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
@@ -723,9 +758,9 @@ def main():
     try:
         if args.workload == "prefill":
             run_prefill(args, rank, world, local_rank)
-        elif args.workload == "e2e":
+        elif args.workload in ("e2e", "c5"):
             if args.steps > 3:
-                args.steps = 1      # one generate() of the whole C4 request set per step
+                args.steps = 1      # one generate() of the whole request set per step
             run_e2e(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)

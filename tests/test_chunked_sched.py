@@ -62,10 +62,16 @@ def _drive(prompt_lens, max_new, budget, max_seqs, num_blocks, bs, seed=0, eos=N
                     eos if eos is not None else -1) for n in prompt_lens]
     for r in reqs:
         sched.add(r)
-    trace, preemptions = [], 0
+    trace, preempted = [], []
+    plain = sched._preempt
+
+    def counting(req):
+        preempted.append(req.id)
+        plain(req)
+
+    sched._preempt = counting
     while not sched.is_finished():
         assert len(trace) < 10000, "no progress"
-        before = {r.id: r.num_computed_tokens for r in reqs}
         batch = sched.schedule()
         assert batch, "empty step while requests remain"
         assert sum(n for _, n in batch) <= budget
@@ -75,9 +81,6 @@ def _drive(prompt_lens, max_new, budget, max_seqs, num_blocks, bs, seed=0, eos=N
         for r, n in batch:
             assert n >= 1
             assert r.num_computed_tokens + n <= len(r)
-            # preempted requests restart from 0
-            if r.num_computed_tokens < before[r.id]:
-                preemptions += 1
             blocks = kv.block_ids(r)
             assert len(blocks) * bs >= r.num_computed_tokens + n
             owned += blocks
@@ -97,7 +100,7 @@ def _drive(prompt_lens, max_new, budget, max_seqs, num_blocks, bs, seed=0, eos=N
         assert r.num_completion_tokens == want
         assert r.num_computed_tokens == len(r) - 1
     assert len(kv.free_block_queue) == num_blocks
-    return trace, preemptions
+    return trace, len(preempted)
 
 
 def test_chunked_scheduler_invariants_and_completion():

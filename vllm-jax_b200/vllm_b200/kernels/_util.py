@@ -6,6 +6,7 @@ import torch
 from .. import _native
 
 _workspaces: dict[tuple[int, str], torch.Tensor] = {}
+_retired: list[torch.Tensor] = []
 
 
 def stream_ptr(device: torch.device) -> int:
@@ -40,10 +41,15 @@ def require_dtype(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
 
 
 def workspace(device: torch.device, nbytes: int, tag: str = "decode") -> torch.Tensor:
-    """Per-device, per-tag scratch buffer that only grows (16-byte aligned)."""
+    """Per-device, per-tag scratch buffer that only grows (16-byte aligned).
+
+    A buffer that is outgrown is retired, never freed: a CUDA graph captured
+    while it was current keeps its address and writes there on every replay."""
     key = (device.index if device.index is not None else torch.cuda.current_device(), tag)
     buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes:
+        if buf is not None:
+            _retired.append(buf)
         buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _workspaces[key] = buf
     return buf

@@ -24,14 +24,17 @@ DEFAULT_MASK_VALUE = -0.7 * float(torch.finfo(torch.float32).max)
 
 
 def _launch(q, k_base, v_base, nb, bs, strides, block_tables, lengths, scale, out=None,
-            max_chunks: int = 0):
+            max_chunks: int = 0, ws: torch.Tensor | None = None):
     dev = require_cuda(q, k_base, v_base, block_tables, lengths)
     B, Hq, D = q.shape
     Hkv = strides[3]
     if out is None:
         out = torch.empty_like(q)
     ws_bytes = _native.load().vj_paged_decode_workspace_size(B, Hq, D, max_chunks)
-    ws = workspace(dev, ws_bytes, "decode")
+    if ws is None:
+        ws = workspace(dev, ws_bytes, "decode")
+    elif ws.numel() < ws_bytes or ws.dtype != torch.uint8:
+        raise ValueError(f"decode workspace must be uint8 with >= {ws_bytes} bytes")
     _native.call("vj_paged_decode", q.data_ptr(), k_base.data_ptr(), v_base.data_ptr(),
                  block_tables.data_ptr(), lengths.data_ptr(), out.data_ptr(),
                  B, Hq, Hkv, D, nb, bs, block_tables.shape[1], block_tables.stride(0),
@@ -94,8 +97,11 @@ def decode_paged_attention(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torc
 
 def paged_decode(q: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.Tensor,
                  context_lens: torch.Tensor, scale: float | None = None,
-                 out: torch.Tensor | None = None, max_chunks: int = 0) -> torch.Tensor:
-    """Decode attention straight from the engine cache (2, nb, bs, Hkv, D)."""
+                 out: torch.Tensor | None = None, max_chunks: int = 0,
+                 workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode attention straight from the engine cache (2, nb, bs, Hkv, D).
+    `workspace` (uint8, decode_workspace_bytes(...) long) pins the split-KV
+    scratch to a caller-owned buffer, as CUDA-graph replays need."""
     require_dtype(q, torch.bfloat16, "q")
     require_dtype(kv_cache, torch.bfloat16, "kv_cache")
     require_dtype(block_tables, torch.int32, "block_tables")
@@ -113,4 +119,11 @@ def paged_decode(q: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.Te
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     strides = (k.stride(0), k.stride(1), k.stride(2), Hkv)
-    return _launch(q, k, v, nb, bs, strides, block_tables, context_lens, scale, out, max_chunks)
+    return _launch(q, k, v, nb, bs, strides, block_tables, context_lens, scale, out, max_chunks,
+                   workspace)
+
+
+def decode_workspace_bytes(batch: int, num_q_heads: int, head_dim: int = 128,
+                           max_chunks: int = 0) -> int:
+    return int(_native.load().vj_paged_decode_workspace_size(batch, num_q_heads, head_dim,
+                                                            max_chunks))

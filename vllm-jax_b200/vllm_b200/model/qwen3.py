@@ -198,6 +198,9 @@ class Qwen3Model:
         self.hkv = c.num_key_value_heads // weights.tp_size
         self.d = c.head_dim
         self.scale = 1.0 / math.sqrt(c.head_dim)
+        # split-KV scratch of the decode kernel, owned here so that captured
+        # CUDA graphs keep a valid address (set by the model runner)
+        self.decode_workspace: torch.Tensor | None = None
 
     def _all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         if self.pg is not None and self.w.tp_size > 1:
@@ -257,7 +260,8 @@ class Qwen3Model:
         x = self.embed(meta.input_ids)
 
         def attn(q, kv):
-            return paged_decode(q, kv, meta.block_tables, meta.context_lens, self.scale)
+            return paged_decode(q, kv, meta.block_tables, meta.context_lens, self.scale,
+                                workspace=self.decode_workspace)
 
         x = self._stack(x, kv_caches, meta, attn)
         return F.linear(x, self.w.lm_head)           # compute_logits (qwen3.py:474-477)
@@ -275,7 +279,7 @@ class Qwen3Model:
             out = torch.empty_like(q)
             if nd:
                 paged_decode(q[:nd], kv, meta.block_tables[:nd], meta.context_lens[:nd],
-                             self.scale, out=out[:nd])
+                             self.scale, out=out[:nd], workspace=self.decode_workspace)
             if S > nd:
                 paged_prefill(q, kv, meta.block_tables[nd:S], meta.cu_seqlens_q[nd:S + 1],
                               meta.context_lens[nd:S], max_seqlen_q=meta.max_new,

@@ -128,6 +128,9 @@ class Engine:
         if not batch:
             raise RuntimeError("chunked scheduler made no progress (pool too small?)")
         st = self.stats
+        all_decode = all(n == 1 and r.num_computed_tokens + 1 == len(r) for r, n in batch)
+        if all_decode:
+            st["decode_ctx_tokens"] += sum(len(r) for r, _ in batch)
         if self.trace is not None:
             self.trace.append({"batch": [(r.id, r.num_computed_tokens, n) for r, n in batch],
                                "blocks": {r.id: self.kv.block_ids(r) for r, _ in batch}})
@@ -135,9 +138,8 @@ class Engine:
         self.scheduler.postprocess(batch, sampled)
         st["steps"] += 1
         st["decode_tokens"] += len(sampled)
-        st["decode_steps"] += 1
+        st["decode_steps"] += 1 if all_decode else 0
         st["prefill_tokens"] += sum(n for r, n in batch if n > 1 or r.id not in sampled)
-        st["decode_ctx_tokens"] += sum(r.num_computed_tokens for r, _ in batch)
         done = []
         for r, _ in batch:
             if r.is_finished():

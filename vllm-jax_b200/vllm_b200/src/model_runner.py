@@ -18,6 +18,7 @@ import torch
 
 from .. import _native
 from ..config import Config
+from ..kernels.decode_paged_attention import decode_workspace_bytes
 from ..kernels.metadata import DecodeMeta, DeviceTables, bucket_size
 from ..model.qwen3 import Qwen3Config, Qwen3Model, Qwen3Weights
 from .kv_cache_manager import KVCacheManager
@@ -43,6 +44,13 @@ class ModelRunner:
         self.width = config.max_blocks_per_seq
         self.weights = weights or Qwen3Weights(model_cfg, device, seed, tp_rank, tp_size)
         self.model = Qwen3Model(self.weights, process_group)
+        # one decode workspace for the largest batch bucket, allocated before
+        # any graph capture and never replaced
+        self.model.decode_workspace = torch.empty(
+            max(decode_workspace_bytes(bucket_size(max(config.max_num_seqs, 1)),
+                                       model_cfg.num_attention_heads // tp_size,
+                                       model_cfg.head_dim), 16),
+            dtype=torch.uint8, device=device)
         hkv = model_cfg.num_key_value_heads // tp_size
         shape = (2, kv_cache_manager.num_blocks, config.block_size, hkv, model_cfg.head_dim)
         # zero-initialised like the reference's pool (model_runner.py:190-199)

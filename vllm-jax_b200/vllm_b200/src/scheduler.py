@@ -95,7 +95,8 @@ class ChunkedScheduler:
     most max_num_seqs requests. Running requests come first, in order: one
     token for a request whose known tokens are all cached (decode), else the
     next chunk of its prompt; then waiting requests start their prompt with
-    whatever budget is left. A request samples a token when a step processes
+    whatever budget is left, admitted only while the pool holds all their
+    known tokens plus a 1% watermark (their blocks are taken at admission). A request samples a token when a step processes
     its last known token. When the pool runs dry the request at the tail of
     `running` is preempted (blocks freed, recomputed from scratch later) unless
     a shorter chunk still fits. Finished requests always release their blocks."""
@@ -104,6 +105,7 @@ class ChunkedScheduler:
         self.max_num_batched_tokens = config.max_num_batched_tokens
         self.max_num_seqs = config.max_num_seqs
         self.kv_cache_manager = kv_cache_manager
+        self.watermark_blocks = max(1, kv_cache_manager.num_blocks // 100)
         self.waiting: deque[Request] = deque()
         self.running: deque[Request] = deque()
         self.finished_requests: list[Request] = []
@@ -150,13 +152,17 @@ class ChunkedScheduler:
             i += 1
         while self.waiting and len(out) < self.max_num_seqs and budget > 0:
             req = self.waiting[0]
-            n = min(len(req), budget)
-            if not kv.can_grow(req, n):
+            # admission reserves blocks for every known token (its later chunks
+            # never allocate) and keeps a watermark free for decode growth, so
+            # that a new prompt does not immediately preempt running requests
+            need = -(-len(req) // kv.block_size)
+            if need + self.watermark_blocks > len(kv.free_block_queue):
                 break
+            n = min(len(req), budget)
             self.waiting.popleft()
             req.status = Status.RUNNING
             self.running.append(req)
-            kv.grow(req, n)
+            kv.grow(req, len(req))
             out.append((req, n))
             budget -= n
         return out
