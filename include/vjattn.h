@@ -255,6 +255,25 @@ VJ_API vj_status vj_argmax_append(const void *logits, int64_t row_stride,
                                   int32_t token_stride, const int32_t *seq_slots,
                                   const int32_t *seq_lens, cudaStream_t stream);
 
+/* Sampling, vllm/sampler.py:7-42 (the reference samples one request at a
+ * time with one device->host copy each; this is one launch per batch).
+ * Per row r: temperature[r] <= 0 -> argmax of the raw logits (first index on
+ * ties). Otherwise x = bf16(logit / temperature[r]); top_k[r] > 0 keeps the
+ * top_k largest x (equal values: lower index first); top_p[r] < 1 then keeps,
+ * in (x desc, index asc) order, the tokens whose cumulative softmax
+ * probability over the kept set is <= top_p[r] (the first always kept); the
+ * token is drawn from softmax(x) over the kept set by Gumbel-max with
+ * Philox4x32-10 keyed by seeds[2r], seeds[2r+1] and counter (vocab index,
+ * seq_lens[r] or 0). num_kept (optional) receives the kept-set size.
+ * token_table as in vj_argmax_append. logits must be 16-byte aligned with a
+ * row stride that is a multiple of 8 elements. */
+VJ_API vj_status vj_sample(const void *logits, int64_t row_stride, int32_t num_rows,
+                           int32_t vocab, const float *temperature, const int32_t *top_k,
+                           const float *top_p, const uint32_t *seeds,
+                           int32_t *out_tokens, int32_t *num_kept, int32_t *token_table,
+                           int32_t token_stride, const int32_t *seq_slots,
+                           const int32_t *seq_lens, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

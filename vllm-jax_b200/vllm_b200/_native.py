@@ -59,6 +59,8 @@ PROTOTYPES: dict[str, tuple] = {
     "vj_scatter_rows": (c_int, [c_vp, c_vp, c_i32, c_vp, c_i32, c_i32, c_vp, c_vp, c_vp]),
     "vj_argmax_append": (c_int, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_i32, c_vp, c_vp,
                                  c_vp]),
+    "vj_sample": (c_int, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                          c_i32, c_vp, c_vp, c_vp]),
 }
 
 # vj_status codes (include/vjattn.h)

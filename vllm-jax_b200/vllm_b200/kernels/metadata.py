@@ -76,6 +76,7 @@ class DeviceTables:
         self.blocks = torch.zeros((max_slots, max_blocks), dtype=torch.int32, device=device)
         self.num_blocks = torch.zeros(max_slots, dtype=torch.int32, device=device)
         self.error = torch.zeros(1, dtype=torch.int32, device=device)
+        self._last_extra = None
         self._pinned = torch.empty(1 << 16, dtype=torch.int32).pin_memory()
         self._staging = torch.empty(1 << 16, dtype=torch.int32, device=device)
 
@@ -118,12 +119,19 @@ class DeviceTables:
         self._scatter([(slot, 0, blk) for slot, blk in rows], self.blocks, self.num_blocks,
                       self.max_blocks)
 
-    def _lists(self, slots, lens):
-        arr = self._upload(np.concatenate([np.asarray(slots, np.int32),
-                                           np.asarray(lens, np.int32)]))
+    def _lists(self, slots, lens, extra: np.ndarray | None = None):
+        parts = [np.asarray(slots, np.int32), np.asarray(lens, np.int32)]
+        if extra is not None:
+            parts.append(np.asarray(extra).view(np.int32).ravel())
+        arr = self._upload(np.concatenate(parts))
         n = len(slots)
         self._last = (arr[:n], arr[n:2 * n])
+        self._last_extra = arr[2 * n:] if extra is not None else None
         return self._last
+
+    def last_extra(self) -> torch.Tensor | None:
+        """Device copy of the `extra` words of the latest build_decode call."""
+        return self._last_extra
 
     def last_lists(self) -> tuple[torch.Tensor, torch.Tensor]:
         """Device (slots, lens) of the latest build_* call; valid until the next upload."""
@@ -151,7 +159,8 @@ class DeviceTables:
                            d_lens.clone(), S, total)
 
     def build_ranges(self, slots: list[int], starts: list[int], ns: list[int], width: int,
-                     sample: list[int], bucket_batch: int | None = None) -> RangesMeta:
+                     sample: list[int], bucket_batch: int | None = None,
+                     extra: np.ndarray | None = None) -> RangesMeta:
         """Metadata of a mixed batch (chunked prefill + decode) with vj_build_metadata
         in ranges mode: sequence s contributes positions [starts[s], starts[s] +
         ns[s]); tokens are padded to a power of two like prefill. `sample` lists
@@ -166,11 +175,13 @@ class DeviceTables:
             np.asarray(slots, np.int32), np.asarray(starts, np.int32),
             np.asarray(ns, np.int32), (ends[sample] - 1).astype(np.int32),
             np.asarray(slots, np.int32)[sample],
-            (np.asarray(starts, np.int64) + np.asarray(ns, np.int64))[sample].astype(np.int32)]))
+            (np.asarray(starts, np.int64) + np.asarray(ns, np.int64))[sample].astype(np.int32)]
+            + ([np.asarray(extra).view(np.int32).ravel()] if extra is not None else [])))
         d_slots, d_starts, d_ns = arr[:S], arr[S:2 * S], arr[2 * S:3 * S]
         K = sample.size
         rows = arr[3 * S:3 * S + K]
         s_slots, s_lens = arr[3 * S + K:3 * S + 2 * K], arr[3 * S + 2 * K:3 * S + 3 * K]
+        self._last_extra = arr[3 * S + 3 * K:] if extra is not None else None
         dev = self.device
         ids = torch.empty(bt, dtype=torch.int32, device=dev)
         pos = torch.empty_like(ids)
@@ -188,12 +199,15 @@ class DeviceTables:
                           s_slots, s_lens)
 
     def build_decode(self, slots: list[int], lens: list[int], width: int,
-                     last_block_slot: bool = True, out: DecodeMeta | None = None) -> DecodeMeta:
+                     last_block_slot: bool = True, out: DecodeMeta | None = None,
+                     extra: np.ndarray | None = None) -> DecodeMeta:
         """Decode metadata for len(slots) rows padded to a power of two; with
-        `out`, written into its (static, CUDA-graph) buffers of that bucket."""
+        `out`, written into its (static, CUDA-graph) buffers of that bucket.
+        `extra` (32-bit words, e.g. sampling parameters) rides the same
+        upload; see last_extra()."""
         B = len(slots)
         bb = bucket_size(B)
-        d_slots, d_lens = self._lists(slots, lens)
+        d_slots, d_lens = self._lists(slots, lens, extra)
         dev = self.device
         if out is not None:
             if out.input_ids.numel() != bb or out.block_tables.shape[1] != width:

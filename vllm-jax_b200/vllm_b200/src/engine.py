@@ -157,13 +157,12 @@ class Engine:
             sampling_params = SamplingParams(**{k: v for k, v in kwargs.items() if k in names})
         params = (sampling_params if isinstance(sampling_params, list)
                   else [sampling_params] * len(prompts))
-        for sp in params:
-            if sp.temperature > 0:
-                raise NotImplementedError("only greedy decoding (temperature <= 0) is built; "
-                                          "the top-k/top-p sampler is out of scope")
         reqs = []
-        for p, sp in zip(prompts, params):
+        for i, (p, sp) in enumerate(zip(prompts, params)):
             r = Request(self.preprocess(p), sp, self.eos_token_id)
+            # sampled tokens depend on (seed, prompt index, position) only, not
+            # on how requests were batched
+            r.sample_stream = i
             reqs.append(r)
             self.add_request(r)
         while not self.scheduler.is_finished():

@@ -14,12 +14,14 @@ from __future__ import annotations
 
 import time
 
+import numpy as np
 import torch
 
 from .. import _native
 from ..config import Config
 from ..kernels.decode_paged_attention import decode_workspace_bytes
 from ..kernels.metadata import DecodeMeta, DeviceTables, bucket_size
+from ..kernels.sampler import sample
 from ..model.qwen3 import Qwen3Config, Qwen3Model, Qwen3Weights
 from .kv_cache_manager import KVCacheManager
 from .request import Request
@@ -28,6 +30,24 @@ from .request import Request
 def kv_cache_bytes_per_block(mcfg: Qwen3Config, block_size: int, tp_size: int) -> int:
     return (mcfg.num_hidden_layers * 2 * block_size * (mcfg.num_key_value_heads // tp_size)
             * mcfg.head_dim * 2)
+
+
+def sampling_words(requests: list[Request]) -> np.ndarray | None:
+    """Per-row sampling parameters as 32-bit words for one upload:
+    temperature f32 [n], top_k i32 [n], top_p f32 [n], seeds u32 [n, 2].
+    None when every request is greedy (the argmax kernel is used then)."""
+    sps = [r.sampling_params for r in requests]
+    if all(sp.temperature <= 0 for sp in sps):
+        return None
+    n = len(requests)
+    w = np.empty(5 * n, np.uint32)
+    w[:n] = np.asarray([sp.temperature for sp in sps], np.float32).view(np.uint32)
+    w[n:2 * n] = np.asarray([sp.top_k for sp in sps], np.int64).astype(np.uint32)
+    w[2 * n:3 * n] = np.asarray([sp.top_p for sp in sps], np.float32).view(np.uint32)
+    seeds = np.asarray([(sp.seed & 0xFFFFFFFF, r.sample_stream & 0xFFFFFFFF)
+                        for sp, r in zip(sps, requests)], np.uint64).astype(np.uint32)
+    w[3 * n:] = seeds.ravel()
+    return w
 
 
 class ModelRunner:
@@ -126,23 +146,35 @@ class ModelRunner:
                 break
             b *= 2
 
+    def _draw(self, logits: torch.Tensor, d_slots: torch.Tensor, d_lens: torch.Tensor,
+              words: torch.Tensor | None) -> torch.Tensor:
+        """Next token of each row (stored into the device token table too):
+        argmax when all rows are greedy, else the sampling kernel."""
+        if words is None:
+            return self.tables.argmax_append(logits, d_slots, d_lens)
+        n = logits.shape[0]
+        return sample(logits, words[:n].view(torch.float32), words[n:2 * n],
+                      words[2 * n:3 * n].view(torch.float32), words[3 * n:5 * n],
+                      positions=d_lens, token_table=self.tables.tokens, slots=d_slots)
+
     def decode(self, requests: list[Request]) -> list[int]:
         slots = [r.slot for r in requests]
         lens = [len(r) for r in requests]
         B = len(requests)
         bb = bucket_size(B)
+        words = sampling_words(requests)
         if self.use_cuda_graphs:
             graph, meta, logits = self._decode_graph(bb)
             self.tables.build_decode(slots, lens, self.width, out=meta,
-                                     last_block_slot=self.config.compat)
+                                     last_block_slot=self.config.compat, extra=words)
             graph.replay()
             _native.launch_count += self.graph_launches[bb]
         else:
             meta = self.tables.build_decode(slots, lens, self.width,
-                                            last_block_slot=self.config.compat)
+                                            last_block_slot=self.config.compat, extra=words)
             logits = self.model.forward_decode(meta, self.kv_caches)
         d_slots, d_lens = self.tables.last_lists()
-        toks = self.tables.argmax_append(logits[:B], d_slots, d_lens)
+        toks = self._draw(logits[:B], d_slots, d_lens, self.tables.last_extra())
         host = self._tok_host if B <= self._tok_host.numel() else torch.empty(
             B, dtype=torch.int32).pin_memory()
         host[:B].copy_(toks, non_blocking=True)
@@ -216,14 +248,16 @@ class ModelRunner:
             rows = [batch[i] for i in order]
             nd = sum(1 for _, n in rows if n == 1)
             pick = [i for i, (r, n) in enumerate(rows) if r.num_computed_tokens + n == len(r)]
+            words = sampling_words([rows[i][0] for i in pick]) if pick else None
             meta = self.tables.build_ranges([r.slot for r, _ in rows],
                                             [r.num_computed_tokens for r, _ in rows],
-                                            [n for _, n in rows], self.width, pick)
+                                            [n for _, n in rows], self.width, pick, extra=words)
             logits = self.model.forward_mixed(meta, self.kv_caches, nd, meta.sample_rows)
             K = len(pick)
             toks = []
             if K:
-                d = self.tables.argmax_append(logits, meta.sample_slots, meta.sample_lens)
+                d = self._draw(logits, meta.sample_slots, meta.sample_lens,
+                               self.tables.last_extra())
                 host = self._tok_host if K <= self._tok_host.numel() else torch.empty(
                     K, dtype=torch.int32).pin_memory()
                 host[:K].copy_(d, non_blocking=True)

@@ -34,6 +34,9 @@ class Request:
         self.num_completion_tokens = 0
         self.slot = -1
         self.num_computed_tokens = 0   # chunked mode: positions whose KV is cached
+        # sampling stream: Philox key (seed, stream id); the engine sets the
+        # stream id to the request's index in its generate() call
+        self.sample_stream = self.id
 
     def is_finished(self) -> bool:
         return self.status == Status.FINISHED
