@@ -274,6 +274,42 @@ VJ_API vj_status vj_sample(const void *logits, int64_t row_stride, int32_t num_r
                            int32_t token_stride, const int32_t *seq_slots,
                            const int32_t *seq_lens, cudaStream_t stream);
 
+/* ---- tensor parallelism over NVLink peer memory (no counterpart in the
+ * reference, which runs on one device; its layer dataflow
+ * vllm/model/qwen3.py:375-389 is what the fused op computes) ---- */
+#define VJ_TP_MAX_RANKS 8
+#define VJ_IPC_HANDLE_BYTES 64
+
+/* Grid of vj_allreduce_add_rmsnorm on this device (2 x SMs); every rank must
+ * report the same value. */
+VJ_API int32_t vj_tp_grid(void);
+/* Bytes of the flag region at the start of a rank's communication memory:
+ * flags [world][grid] u32, epochs [grid] u32, one error word. */
+VJ_API size_t vj_tp_flags_bytes(int32_t world);
+/* cudaMalloc'd, zeroed device memory that can be shared with
+ * vj_ipc_get_handle (a torch caching-allocator block cannot). */
+VJ_API vj_status vj_comm_alloc(size_t bytes, void **ptr);
+VJ_API vj_status vj_comm_free(void *ptr);
+/* cudaIpc handle (VJ_IPC_HANDLE_BYTES bytes) of a vj_comm_alloc pointer, and
+ * its mapping in another process (peer access enabled lazily). */
+VJ_API vj_status vj_ipc_get_handle(void *ptr, void *handle_out);
+VJ_API vj_status vj_ipc_open_handle(const void *handle, void **ptr);
+VJ_API vj_status vj_ipc_close_handle(void *ptr);
+
+/* out = residual + sum over ranks of bufs[r][rows, hidden] (fp32 sum in rank
+ * order, rounded to bf16, added in bf16); y = RMSNorm(out) * weight as
+ * vj_add_rmsnorm. bufs[r] is rank r's partial (peer pointers, own included);
+ * peer_flags[r] the flag region of rank r; flags this rank's own. Each CTA
+ * signals its counterpart on every peer and waits for theirs (bounded: 2 s;
+ * on timeout the error word of `flags` is set and the CTA returns). All ranks
+ * must make the same sequence of calls; a buffer may be rewritten only after
+ * the next call on it has been made by every rank (use two buffers in
+ * alternation). residual / residual_out may be NULL. */
+VJ_API vj_status vj_allreduce_add_rmsnorm(
+    const void *const *bufs, uint32_t *const *peer_flags, uint32_t *flags, int32_t rank,
+    int32_t world, const void *residual, const void *weight, void *residual_out, void *y,
+    int64_t rows, int32_t hidden, float eps, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,78 @@
+"""Fused all-reduce + residual add + RMSNorm (vj_allreduce_add_rmsnorm) on
+ONE GPU: the ranks' communication regions all live on this device and the
+flags a CTA waits on are pre-set, so a single launch runs with nothing to
+wait for (kernels that wait on one another never run as separate launches on
+one GPU). Checks the arithmetic bit for bit: fp32 sum of the partials in rank
+order, rounded to bf16, then exactly vj_add_rmsnorm; every rank's result is
+identical. The cross-GPU path is covered by test_tp_nvlink_gpu.py."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _region(lib, world, rows, hidden):
+    from vllm_b200 import _native
+    flag_bytes = int(lib.vj_tp_flags_bytes(world))
+    buf_bytes = (rows * hidden * 2 + 4095) // 4096 * 4096
+    p = ctypes.c_void_p()
+    _native.check(lib.vj_comm_alloc(flag_bytes + 2 * buf_bytes, ctypes.byref(p)))
+    return p.value, flag_bytes, buf_bytes
+
+
+@pytest.mark.parametrize("world,rows,hidden", [(1, 7, 1024), (2, 64, 4096), (4, 33, 5120),
+                                               (8, 5, 2048)])
+def test_fused_allreduce_matches_sum_then_add_rmsnorm(world, rows, hidden):
+    from vllm_b200 import _native
+    from vllm_b200.kernels.fused import add_rmsnorm
+    from vllm_b200.src.tp_comm import device_view
+    lib = _native.load()
+    dev = torch.device("cuda", 0)
+    G = int(lib.vj_tp_grid())
+    regions = [_region(lib, world, rows, hidden) for _ in range(world)]
+    g = torch.Generator(device="cpu").manual_seed(world * 100 + rows)
+    parts = [torch.randn(rows, hidden, generator=g).bfloat16().to(dev) for _ in range(world)]
+    x = torch.randn(rows, hidden, generator=g).bfloat16().to(dev)
+    w = (1 + 0.1 * torch.randn(hidden, generator=g)).bfloat16().to(dev)
+    site = 1
+    for (base, fb, bb), pt in zip(regions, parts):
+        device_view(base + fb + site * bb, (rows, hidden), torch.bfloat16, dev).copy_(pt)
+        # flags this rank waits on: already far past any epoch
+        device_view(base, (world * G,), torch.int32, dev).fill_(1 << 30)
+    s = torch.zeros(rows, hidden, dtype=torch.float32, device=dev)
+    for pt in parts:
+        s += pt.float()
+    ref_x, ref_y = add_rmsnorm(s.bfloat16(), w, 1e-6, residual=x)
+    bufs = (ctypes.c_void_p * world)(*[b + fb + site * bb for b, fb, bb in regions])
+    flags = (ctypes.c_void_p * world)(*[b for b, _, _ in regions])
+    for rank in range(world):
+        x_out = torch.empty_like(x)
+        y = torch.empty_like(x)
+        _native.call("vj_allreduce_add_rmsnorm", ctypes.cast(bufs, ctypes.c_void_p),
+                     ctypes.cast(flags, ctypes.c_void_p), ctypes.c_void_p(regions[rank][0]),
+                     rank, world, x.data_ptr(), w.data_ptr(), x_out.data_ptr(), y.data_ptr(),
+                     rows, hidden, 1e-6, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        err = device_view(regions[rank][0] + (world + 1) * G * 4, (1,), torch.int32, dev)
+        assert int(err.item()) == 0
+        assert torch.equal(x_out, ref_x), f"rank {rank}: residual differs"
+        assert torch.equal(y, ref_y), f"rank {rank}: normed output differs"
+    for base, _, _ in regions:
+        _native.check(lib.vj_comm_free(ctypes.c_void_p(base)))
+
+
+def test_fused_allreduce_rejects_bad_arguments():
+    from vllm_b200 import _native
+    lib = _native.load()
+    null = (ctypes.c_void_p * 2)(None, None)
+    st = lib.vj_allreduce_add_rmsnorm(ctypes.cast(null, ctypes.c_void_p),
+                                      ctypes.cast(null, ctypes.c_void_p), None, 0, 9, None,
+                                      None, None, None, 4, 1024, 1e-6, None)
+    assert st == _native.VJ_ERR_INVALID_ARGUMENT
+    st = lib.vj_allreduce_add_rmsnorm(ctypes.cast(null, ctypes.c_void_p),
+                                      ctypes.cast(null, ctypes.c_void_p), None, 0, 2, None,
+                                      None, None, None, 4, 10000, 1e-6, None)
+    assert st == _native.VJ_ERR_UNSUPPORTED

@@ -59,6 +59,15 @@ PROTOTYPES: dict[str, tuple] = {
     "vj_scatter_rows": (c_int, [c_vp, c_vp, c_i32, c_vp, c_i32, c_i32, c_vp, c_vp, c_vp]),
     "vj_argmax_append": (c_int, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_i32, c_vp, c_vp,
                                  c_vp]),
+    "vj_tp_grid": (c_i32, []),
+    "vj_tp_flags_bytes": (c_sz, [c_i32]),
+    "vj_comm_alloc": (c_int, [c_sz, c_vp]),
+    "vj_comm_free": (c_int, [c_vp]),
+    "vj_ipc_get_handle": (c_int, [c_vp, c_vp]),
+    "vj_ipc_open_handle": (c_int, [c_vp, c_vp]),
+    "vj_ipc_close_handle": (c_int, [c_vp]),
+    "vj_allreduce_add_rmsnorm": (c_int, [c_vp, c_vp, c_vp, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp,
+                                         c_i64, c_i32, ctypes.c_float, c_vp]),
     "vj_sample": (c_int, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                           c_i32, c_vp, c_vp, c_vp]),
 }

@@ -23,6 +23,10 @@ class Config:
     # forward with decode rows (not in the reference). Implies compat=False
     # behaviour: position-addressed slots and blocks freed on finish.
     enable_chunked_prefill: bool = False
+    # Under tensor parallelism: "nvlink" reduces decode-sized batches with the
+    # fused peer-memory kernel (CUDA-graph capturable), "nccl" always uses
+    # torch.distributed all-reduce (decode then runs eagerly).
+    tp_allreduce: str = "nvlink"
 
     @property
     def max_len(self) -> int:

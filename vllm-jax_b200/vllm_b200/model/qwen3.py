@@ -189,10 +189,13 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
 class Qwen3Model:
     """Forward passes of one rank. kv_caches[l]: (2, num_blocks, bs, Hkv_l, D) bf16."""
 
-    def __init__(self, weights: Qwen3Weights, process_group=None):
+    def __init__(self, weights: Qwen3Weights, process_group=None, tp_comm=None):
         self.w = weights
         self.cfg = weights.cfg
         self.pg = process_group
+        # NVLink communicator (src/tp_comm.py): row-parallel GEMMs of up to
+        # tp_comm.max_rows rows reduce through the fused peer-memory kernel
+        self.tp_comm = tp_comm
         c = self.cfg
         self.hq = c.num_attention_heads // weights.tp_size
         self.hkv = c.num_key_value_heads // weights.tp_size
@@ -207,11 +210,25 @@ class Qwen3Model:
             torch.distributed.all_reduce(x, group=self.pg)
         return x
 
+    def _reduce_add_norm(self, a: torch.Tensor, w: torch.Tensor, x: torch.Tensor,
+                         w_norm: torch.Tensor, site: int):
+        """Row-parallel GEMM a @ w.T summed over ranks, added to the residual x,
+        then RMSNorm: returns (new residual, normed). Under tensor parallelism
+        the GEMM writes into the NVLink buffer and one kernel reduces, adds and
+        normalises; otherwise NCCL all-reduce (or nothing) + vj_add_rmsnorm."""
+        T = a.shape[0]
+        eps = self.cfg.rms_norm_eps
+        c = self.tp_comm
+        if c is not None and T <= c.max_rows:
+            torch.mm(a, w.t(), out=c.buffer(site, T))
+            return c.allreduce_add_rmsnorm(site, T, x, w_norm, eps)
+        d = self._all_reduce(F.linear(a, w))
+        return add_rmsnorm(d, w_norm, eps, residual=x)
+
     def _layer(self, l: int, x: torch.Tensor, h: torch.Tensor, kv_cache: torch.Tensor, meta,
-               attn_fn):
+               attn_fn, w_next: torch.Tensor):
         """x: residual stream entering layer l; h = input_layernorm(x). Returns
-        (x + attn, post-attention-normed) -> MLP output d; the caller fuses
-        x + d with the next norm."""
+        (x after the layer, h = the next norm of it, with weight w_next)."""
         lw = self.w.layers[l]
         c = self.cfg
         T = x.shape[0]
@@ -222,20 +239,19 @@ class Qwen3Model:
                                  meta.slot_mapping, meta.positions, lw.q_norm, lw.k_norm,
                                  eps=c.rms_norm_eps, rope_theta=c.rope_theta)
         o = attn_fn(q, kv_cache).reshape(T, self.hq * self.d)
-        o = self._all_reduce(F.linear(o, lw.w_o))
-        x, h = add_rmsnorm(o, lw.ln2, c.rms_norm_eps, residual=x)   # attn_output += x; norm
+        # attn_output += x; post_attention_layernorm   (qwen3.py:375-389)
+        x, h = self._reduce_add_norm(o, lw.w_o, x, lw.ln2, 0)
         m = silu_mul(F.linear(h, lw.w_gate_up))
-        d = self._all_reduce(F.linear(m, lw.w_down))
-        return x, d
+        # outputs = residual + mlp; next input_layernorm (or the final norm)
+        return self._reduce_add_norm(m, lw.w_down, x, w_next, 1)
 
     def _stack(self, x: torch.Tensor, kv_caches, meta, attn_fn) -> torch.Tensor:
         c = self.cfg
         L = c.num_hidden_layers
         h = add_rmsnorm(x, self.w.layers[0].ln1, c.rms_norm_eps)
         for l in range(L):
-            x, d = self._layer(l, x, h, kv_caches[l], meta, attn_fn)
             w_next = self.w.layers[l + 1].ln1 if l + 1 < L else self.w.norm
-            x, h = add_rmsnorm(d, w_next, c.rms_norm_eps, residual=x)  # outputs = residual + mlp
+            x, h = self._layer(l, x, h, kv_caches[l], meta, attn_fn, w_next)
         return h    # final norm applied
 
     def embed(self, input_ids: torch.Tensor) -> torch.Tensor:

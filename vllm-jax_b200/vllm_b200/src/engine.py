@@ -73,6 +73,16 @@ class Engine:
                 self.config = config = dataclasses.replace(config, compat=False)
             if num_blocks < config.max_blocks_per_seq:
                 raise ValueError("chunked prefill needs a pool of at least max_model_len tokens")
+        self.tp_comm = None
+        if self.tp_size > 1 and config.tp_allreduce == "nvlink":
+            from ..kernels.metadata import bucket_size
+            from .tp_comm import TPComm
+            self.tp_comm = TPComm(process_group or torch.distributed.group.WORLD, self.tp_rank,
+                                  self.tp_size, device,
+                                  max(1024, bucket_size(max(config.max_num_seqs, 1))),
+                                  self.mcfg.hidden_size)
+        elif config.tp_allreduce not in ("nvlink", "nccl"):
+            raise ValueError("tp_allreduce must be 'nvlink' or 'nccl'")
         self.kv = KVCacheManager(num_blocks, config.block_size)
         self.scheduler = (ChunkedScheduler(config, self.kv) if config.enable_chunked_prefill
                           else Scheduler(config, self.kv))
@@ -80,7 +90,7 @@ class Engine:
         self.runner = ModelRunner(config, self.mcfg, self.kv, device, tp_rank=self.tp_rank,
                                   tp_size=self.tp_size, process_group=process_group,
                                   weights=self.weights, max_slots=max_slots,
-                                  use_cuda_graphs=use_cuda_graphs)
+                                  use_cuda_graphs=use_cuda_graphs, tp_comm=self.tp_comm)
         self.live: dict[int, Request] = {}
         self.stats = {"steps": 0, "decode_tokens": 0, "prefill_tokens": 0, "decode_steps": 0,
                       "decode_s": 0.0, "prefill_s": 0.0, "decode_ctx_tokens": 0,
@@ -167,6 +177,8 @@ class Engine:
             self.add_request(r)
         while not self.scheduler.is_finished():
             self.step()
+        if self.tp_comm is not None and self.tp_comm.failed():
+            raise RuntimeError("tensor-parallel all-reduce timed out waiting for a peer rank")
         outs = []
         for r in reqs:
             comp = r.token_ids[r.num_prompt_tokens:]

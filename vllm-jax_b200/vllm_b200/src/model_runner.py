@@ -55,7 +55,7 @@ class ModelRunner:
     def __init__(self, config: Config, model_cfg: Qwen3Config, kv_cache_manager: KVCacheManager,
                  device: torch.device, *, tp_rank: int = 0, tp_size: int = 1,
                  process_group=None, seed: int = 0, weights: Qwen3Weights | None = None,
-                 max_slots: int = 1024, use_cuda_graphs: bool = True):
+                 max_slots: int = 1024, use_cuda_graphs: bool = True, tp_comm=None):
         self.config = config
         self.mcfg = model_cfg
         self.kv = kv_cache_manager
@@ -63,7 +63,7 @@ class ModelRunner:
         self.block_size = config.block_size
         self.width = config.max_blocks_per_seq
         self.weights = weights or Qwen3Weights(model_cfg, device, seed, tp_rank, tp_size)
-        self.model = Qwen3Model(self.weights, process_group)
+        self.model = Qwen3Model(self.weights, process_group, tp_comm)
         # one decode workspace for the largest batch bucket, allocated before
         # any graph capture and never replaced
         self.model.decode_workspace = torch.empty(
@@ -79,9 +79,12 @@ class ModelRunner:
         self.tables = DeviceTables(max_slots, config.max_len, self.width, config.block_size,
                                    device)
         self.free_slots = list(range(max_slots - 1, -1, -1))
-        # Collectives of torch.distributed are not captured into CUDA graphs
-        # here: with tensor parallelism the decode step runs eagerly.
-        self.use_cuda_graphs = use_cuda_graphs and tp_size == 1
+        # Collectives of torch.distributed are not captured into CUDA graphs:
+        # with tensor parallelism decode steps are captured only when the
+        # NVLink communicator reduces every decode bucket.
+        max_bucket = bucket_size(max(config.max_num_seqs, 1))
+        self.use_cuda_graphs = use_cuda_graphs and (
+            tp_size == 1 or (tp_comm is not None and tp_comm.max_rows >= max_bucket))
         self.graphs: dict[int, tuple[torch.cuda.CUDAGraph, DecodeMeta, torch.Tensor]] = {}
         self.graph_launches: dict[int, int] = {}
         self._tok_host = torch.empty(max(config.max_num_seqs, 1), dtype=torch.int32).pin_memory()
