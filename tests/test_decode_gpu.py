@@ -58,7 +58,10 @@ def test_paged_decode_matches_oracle(B, Hq, Hkv, bs, lens):
     q, cache, bt, ln = _make(B, Hq, Hkv, lens, nb, bs, width, seed=B * 100 + Hq)
     scale = 1.0 / math.sqrt(128)
     ref = oatt.decode_attention(q, cache[0], cache[1], bt, ln, scale)
-    out = paged_decode(_t(q), _t(cache), _t(bt, torch.int32), _t(ln, torch.int32), scale)
+    # the output starts as NaN: every row (zero-length ones included) must be written
+    out = torch.full(q.shape, float("nan"), dtype=torch.bfloat16, device="cuda")
+    out = paged_decode(_t(q), _t(cache), _t(bt, torch.int32), _t(ln, torch.int32), scale,
+                       out=out)
     torch.cuda.synchronize()
     got = out.float().cpu().numpy()
     _check(got, ref)

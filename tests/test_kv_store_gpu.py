@@ -45,6 +45,8 @@ def _case(T, Hq, Hkv, nb, bs, seed, pos_max=40000, neg_slots=0, dup_slots=False)
     (300, 32, 8, 64, 16, 0),      # 8B heads
     (129, 64, 8, 32, 16, 5),      # 32B heads
     (50, 4, 1, 16, 32, 0),        # TP-8 shard, block_size 32
+    (33, 8, 1, 16, 16, 2),        # 32B TP-8 shard: k and v rows share a warp
+    (700, 12, 2, 64, 16, 0),      # odd q/k/v boundaries in one pass, many tokens
 ])
 def test_kv_store_bit_exact(T, Hq, Hkv, nb, bs, neg):
     from vllm_b200.kernels.kv_store import kv_store_qknorm_rope

@@ -35,7 +35,7 @@ constexpr int kHalfBytes = kPageTok * 128;   // 16 rows x 64 dims x bf16
 constexpr int kStageBytes = 4 * kHalfBytes;  // K lo/hi + V lo/hi
 constexpr int kCtasPerSm = 2;
 constexpr int kMinChunkPages = 8;
-constexpr int kItemsPerWarp = 16;
+constexpr int kItemsPerWarp = 8;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct Workspace {
@@ -378,16 +378,34 @@ decode_combine_kernel(DecodeArgs a) {
   uint2 *orow = reinterpret_cast<uint2 *>(a.out + ((size_t)b * a.Hq + head) * kD);
   if (n == 1) return;  // written by the chunk kernel
   if (n == 0) { orow[lane] = make_uint2(0u, 0u); return; }
+  // m and l of the chunks, lane-parallel
   float M = -INFINITY;
-  for (int c = c0; c < c1; ++c) M = fmaxf(M, a.ws.part_ml[(size_t)c * a.Hq + head].x);
+  for (int c = c0 + lane; c < c1; c += 32) M = fmaxf(M, a.ws.part_ml[(size_t)c * a.Hq + head].x);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
   float L = 0.f;
-  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int c = c0; c < c1; ++c) {
+  for (int c = c0 + lane; c < c1; c += 32) {
     const float2 ml = a.ws.part_ml[(size_t)c * a.Hq + head];
-    const float w = fast_exp2(ml.x - M);
-    L += w * ml.y;
-    const float4 p = reinterpret_cast<const float4 *>(a.ws.part_o + ((size_t)c * a.Hq + head) * kD)[lane];
-    o.x += w * p.x; o.y += w * p.y; o.z += w * p.z; o.w += w * p.w;
+    L += fast_exp2(ml.x - M) * ml.y;
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  // weighted sum of the partial outputs, four chunks in flight
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int c = c0; c < c1; c += 4) {
+    float4 p[4];
+    float w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const bool in = c + j < c1;
+      const size_t row = (size_t)(in ? c + j : c0) * a.Hq + head;
+      p[j] = reinterpret_cast<const float4 *>(a.ws.part_o + row * kD)[lane];
+      w[j] = in ? fast_exp2(a.ws.part_ml[row].x - M) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      o.x += w[j] * p[j].x; o.y += w[j] * p[j].y; o.z += w[j] * p[j].z; o.w += w[j] * p[j].w;
+    }
   }
   const float inv = 1.f / (L + 1.1920929e-07f);  // + finfo(f32).eps as at :279-280
   orow[lane] = make_uint2(pack_bf16(o.x * inv, o.y * inv), pack_bf16(o.z * inv, o.w * inv));

@@ -7,10 +7,12 @@
 //                                pairs (x[2i], x[2i+1]), bf16 cos/sin)
 //   vllm/model/qwen3.py:105-111  _update_kv_cache (.at[slot].set, mode=drop)
 //
-// Work split: a CTA owns kTokPerCta (2) tokens. It first builds the bf16 cos/sin
-// table of those tokens in shared memory (fp64 trig, rounded once to bf16),
-// then half-warps walk the (token, head) rows: 16 lanes x 16 bytes = one
-// 128-dim head row, so every global access is a coalesced 16-byte vector.
+// Work split: a CTA owns one token. Every half-warp first issues the 16-byte
+// loads of all its (head) rows of that token, so the loads are in flight
+// together, while the first 64 threads compute the token's bf16 cos/sin pairs
+// (fp64 trig, rounded once to bf16) into shared memory; then each half-warp
+// normalises, rotates and stores its rows: 16 lanes x 16 bytes = one 128-dim
+// head row, every global access a coalesced 16-byte vector.
 // HBM-bound: each input byte is read once and each output byte written once.
 #include "../../include/vjattn.h"
 #include "vj_common.cuh"
@@ -21,10 +23,10 @@
 namespace vj {
 namespace {
 
-constexpr int kTokPerCta = 2;   // small CTAs: a decode batch of 512 tokens still fills the GPU
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;   // 16 half-warps
 constexpr int kHeadDim = 128;
 constexpr int kPairs = kHeadDim / 2;
+constexpr int kRowsPerHw = 6;   // rows in flight per half-warp (96 heads per pass)
 
 struct RopeTable {
   float inv_freq[kPairs];  // bf16-valued
@@ -64,109 +66,109 @@ kv_store_qknorm_rope_kernel(const __nv_bfloat16 *__restrict__ q_in,
                             int block_size, int64_t sb, int64_t st, int64_t sh,
                             int64_t qrs, int64_t krs, int64_t vrs,
                             float eps, int flags, RopeTable rope) {
-  __shared__ float2 cs[kTokPerCta][kPairs];
-  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kTokPerCta;
+  __shared__ float2 cs[kPairs];
+  const int64_t t = blockIdx.x;
   const int tid = threadIdx.x;
   const bool do_norm = (flags & VJ_KV_NORM) != 0;
   const bool do_rope = (flags & VJ_KV_ROPE) != 0;
-
-  if (do_rope) {
-    for (int i = tid; i < kTokPerCta * kPairs; i += kThreads) {
-      const int tok = i / kPairs, p = i % kPairs;
-      const int64_t t = t0 + tok;
-      float2 v = make_float2(1.f, 0.f);
-      if (t < T) {
-        // positions.astype(bf16); freqs = bf16(pos * inv_freq)  (qwen3.py:62-65)
-        const float pos = round_bf16(static_cast<float>(positions[t]));
-        const float f = round_bf16(pos * rope.inv_freq[p]);
-        double s, c;
-        sincos(static_cast<double>(f), &s, &c);
-        v = make_float2(bf16_from_f64(c), bf16_from_f64(s));
-      }
-      cs[tok][p] = v;
-    }
-    __syncthreads();
-  }
-
   const int heads = Hq + 2 * Hkv;
   const int hw = tid >> 4;     // half-warp index
   const int l16 = tid & 15;    // lane inside the half-warp: dims 8*l16 .. +7
-  const int ntasks = kTokPerCta * heads;
-  for (int task = hw; task < ntasks; task += kThreads / 16) {
-    const int tok = task / heads;
-    const int hidx = task % heads;
-    const int64_t t = t0 + tok;
-    if (t >= T) break;  // tasks are token-major: the rest are past T too
+  int64_t slot = slots[t];
+  if (slot < 0 && (flags & VJ_KV_WRAP_NEGATIVE)) slot += num_slots;
 
-    const __nv_bfloat16 *src;
-    const __nv_bfloat16 *w = nullptr;
-    int kind;  // 0 = q, 1 = k, 2 = v
-    int h;
-    if (hidx < Hq) {
-      kind = 0; h = hidx; src = q_in + t * qrs + h * kHeadDim; w = q_w;
-    } else if (hidx < Hq + Hkv) {
-      kind = 1; h = hidx - Hq; src = k_in + t * krs + h * kHeadDim; w = k_w;
-    } else {
-      kind = 2; h = hidx - Hq - Hkv; src = v_in + t * vrs + h * kHeadDim;
-    }
-    uint4 raw = *reinterpret_cast<const uint4 *>(src + l16 * 8);
-    uint32_t wd[4] = {raw.x, raw.y, raw.z, raw.w};
-
-    if (kind != 2) {
-      float x[8];
+  for (int base = 0; base < heads; base += 16 * kRowsPerHw) {
+    // ---- 1. loads of this half-warp's rows, all in flight together
+    uint4 raw[kRowsPerHw];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) { x[2 * j] = bf16_lo(wd[j]); x[2 * j + 1] = bf16_hi(wd[j]); }
-      if (do_norm) {
-        // flax RMSNorm: y = bf16(x * (rsqrt(mean(x^2) + eps) * scale)), fp32
-        double ss = 0.0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) ss += static_cast<double>(x[j]) * x[j];
-#pragma unroll
-        for (int o = 8; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float ms = __fdiv_rn(static_cast<float>(ss), static_cast<float>(kHeadDim));
-        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
-        const uint4 wr = *reinterpret_cast<const uint4 *>(w + l16 * 8);
-        const uint32_t ww[4] = {wr.x, wr.y, wr.z, wr.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float m0 = __fmul_rn(inv, bf16_lo(ww[j]));
-          const float m1 = __fmul_rn(inv, bf16_hi(ww[j]));
-          x[2 * j] = round_bf16(__fmul_rn(x[2 * j], m0));
-          x[2 * j + 1] = round_bf16(__fmul_rn(x[2 * j + 1], m1));
-        }
+    for (int k = 0; k < kRowsPerHw; ++k) {
+      const int hidx = base + hw + 16 * k;
+      raw[k] = make_uint4(0u, 0u, 0u, 0u);
+      if (hidx < heads) {
+        const __nv_bfloat16 *src =
+            hidx < Hq ? q_in + t * qrs + hidx * kHeadDim
+            : hidx < Hq + Hkv ? k_in + t * krs + (hidx - Hq) * kHeadDim
+                              : v_in + t * vrs + (hidx - Hq - Hkv) * kHeadDim;
+        raw[k] = *reinterpret_cast<const uint4 *>(src + l16 * 8);
       }
-      if (do_rope) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 c = cs[tok][l16 * 4 + j];  // (cos, sin)
-          const float x1 = x[2 * j], x2 = x[2 * j + 1];
-          // stack((x1*cos - x2*sin, x1*sin + x2*cos), -1): every op rounds to bf16
-          const float a = round_bf16(__fmul_rn(x1, c.x));
-          const float b = round_bf16(__fmul_rn(x2, c.y));
-          const float d = round_bf16(__fmul_rn(x1, c.y));
-          const float e = round_bf16(__fmul_rn(x2, c.x));
-          x[2 * j] = round_bf16(__fsub_rn(a, b));
-          x[2 * j + 1] = round_bf16(__fadd_rn(d, e));
-        }
+    }
+    // ---- 2. the token's cos/sin (first pass only)
+    if (base == 0 && do_rope) {
+      if (tid < kPairs) {
+        // positions.astype(bf16); freqs = bf16(pos * inv_freq)  (qwen3.py:62-65)
+        const float pos = round_bf16(static_cast<float>(positions[t]));
+        const float f = round_bf16(pos * rope.inv_freq[tid]);
+        double s, c;
+        sincos(static_cast<double>(f), &s, &c);
+        cs[tid] = make_float2(bf16_from_f64(c), bf16_from_f64(s));
       }
+      __syncthreads();
+    }
+    // ---- 3. norm, rope, stores
 #pragma unroll
-      for (int j = 0; j < 4; ++j) wd[j] = pack_bf16(x[2 * j], x[2 * j + 1]);
+    for (int k = 0; k < kRowsPerHw; ++k) {
+      const int hidx = base + hw + 16 * k;
+      if (hidx >= heads) break;
+      const int kind = hidx < Hq ? 0 : hidx < Hq + Hkv ? 1 : 2;  // q, k, v
+      const int h = kind == 0 ? hidx : kind == 1 ? hidx - Hq : hidx - Hq - Hkv;
+      uint32_t wd[4] = {raw[k].x, raw[k].y, raw[k].z, raw[k].w};
+      if (kind != 2) {
+        const __nv_bfloat16 *w = kind == 0 ? q_w : k_w;
+        float x[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) { x[2 * j] = bf16_lo(wd[j]); x[2 * j + 1] = bf16_hi(wd[j]); }
+        if (do_norm) {
+          // flax RMSNorm: y = bf16(x * (rsqrt(mean(x^2) + eps) * scale)), fp32
+          double ss = 0.0;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ss += static_cast<double>(x[j]) * x[j];
+          // the two half-warps of a warp may hold different kinds of rows
+          // (odd head counts under tensor parallelism): reduce within the half
+          const unsigned half_mask = 0xffffu << (16 * (hw & 1));
+#pragma unroll
+          for (int o = 8; o >= 1; o >>= 1) ss += __shfl_xor_sync(half_mask, ss, o);
+          const float ms = __fdiv_rn(static_cast<float>(ss), static_cast<float>(kHeadDim));
+          const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+          const uint4 wr = __ldg(reinterpret_cast<const uint4 *>(w + l16 * 8));
+          const uint32_t ww[4] = {wr.x, wr.y, wr.z, wr.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float m0 = __fmul_rn(inv, bf16_lo(ww[j]));
+            const float m1 = __fmul_rn(inv, bf16_hi(ww[j]));
+            x[2 * j] = round_bf16(__fmul_rn(x[2 * j], m0));
+            x[2 * j + 1] = round_bf16(__fmul_rn(x[2 * j + 1], m1));
+          }
+        }
+        if (do_rope) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 c = cs[l16 * 4 + j];  // (cos, sin)
+            const float x1 = x[2 * j], x2 = x[2 * j + 1];
+            // stack((x1*cos - x2*sin, x1*sin + x2*cos), -1): every op rounds to bf16
+            const float a = round_bf16(__fmul_rn(x1, c.x));
+            const float b = round_bf16(__fmul_rn(x2, c.y));
+            const float d = round_bf16(__fmul_rn(x1, c.y));
+            const float e = round_bf16(__fmul_rn(x2, c.x));
+            x[2 * j] = round_bf16(__fsub_rn(a, b));
+            x[2 * j + 1] = round_bf16(__fadd_rn(d, e));
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) wd[j] = pack_bf16(x[2 * j], x[2 * j + 1]);
+      }
+      const uint4 outv = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+      if (kind == 0) {
+        *reinterpret_cast<uint4 *>(q_out + (t * Hq + h) * kHeadDim + l16 * 8) = outv;
+        continue;
+      }
+      if (kind == 1 && k_out != nullptr) {
+        *reinterpret_cast<uint4 *>(k_out + (t * Hkv + h) * kHeadDim + l16 * 8) = outv;
+      }
+      if (slot < 0 || slot >= num_slots) continue;  // mode="drop"
+      const int64_t blk = slot / block_size, off = slot % block_size;
+      __nv_bfloat16 *dst = (kind == 1 ? k_cache : v_cache) + blk * sb + off * st + h * sh;
+      *reinterpret_cast<uint4 *>(dst + l16 * 8) = outv;
     }
-    const uint4 outv = make_uint4(wd[0], wd[1], wd[2], wd[3]);
-
-    if (kind == 0) {
-      *reinterpret_cast<uint4 *>(q_out + (t * Hq + h) * kHeadDim + l16 * 8) = outv;
-      continue;
-    }
-    if (kind == 1 && k_out != nullptr) {
-      *reinterpret_cast<uint4 *>(k_out + (t * Hkv + h) * kHeadDim + l16 * 8) = outv;
-    }
-    int64_t slot = slots[t];
-    if (slot < 0 && (flags & VJ_KV_WRAP_NEGATIVE)) slot += num_slots;
-    if (slot < 0 || slot >= num_slots) continue;  // mode="drop"
-    const int64_t blk = slot / block_size, off = slot % block_size;
-    __nv_bfloat16 *dst = (kind == 1 ? k_cache : v_cache) + blk * sb + off * st + h * sh;
-    *reinterpret_cast<uint4 *>(dst + l16 * 8) = outv;
   }
 }
 
@@ -230,7 +232,7 @@ extern "C" vj_status vj_kv_store_qknorm_rope(
   }
   RopeTable rope;
   build_rope_table(rope_theta, rope.inv_freq);
-  const int64_t grid = (num_tokens + kTokPerCta - 1) / kTokPerCta;
+  const int64_t grid = num_tokens;
   kv_store_qknorm_rope_kernel<<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(
       static_cast<const __nv_bfloat16 *>(q_in), static_cast<const __nv_bfloat16 *>(k_in),
       static_cast<const __nv_bfloat16 *>(v_in), static_cast<const __nv_bfloat16 *>(q_norm_w),
