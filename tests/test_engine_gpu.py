@@ -157,3 +157,48 @@ def test_engine_preemption_completes_without_compat():
                                                 ignore_eos=True))
     assert [len(o) for o in outs] == [27] * 6
     assert eng.stats["prefill_tokens"] > sum(len(p) for p in prompts)   # re-prefills happened
+
+
+def test_engine_loads_a_local_hf_checkpoint(tmp_path):
+    """Config(model=<directory>) reads config.json and the safetensors weights."""
+    import json as _json
+
+    from safetensors.torch import save_file
+
+    from vllm_b200 import Config, SamplingParams
+    from vllm_b200.model.qwen3 import Qwen3Config, Qwen3Weights
+    from vllm_b200.src.engine import Engine
+    cfg = Qwen3Config(vocab_size=512, hidden_size=256, intermediate_size=512,
+                      num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                      tie_word_embeddings=False)
+    w = Qwen3Weights(cfg, torch.device("cpu"), seed=4)
+    D, Hq, Hkv, I = cfg.head_dim, 4, 2, cfg.intermediate_size
+    t = {"model.embed_tokens.weight": w.embed, "model.norm.weight": w.norm,
+         "lm_head.weight": w.lm_head}
+    for l, lw in enumerate(w.layers):
+        p = f"model.layers.{l}."
+        q, k, v = torch.split(lw.w_qkv, [Hq * D, Hkv * D, Hkv * D])
+        g, u = torch.split(lw.w_gate_up, [I, I])
+        t.update({p + "self_attn.q_proj.weight": q, p + "self_attn.k_proj.weight": k,
+                  p + "self_attn.v_proj.weight": v, p + "self_attn.o_proj.weight": lw.w_o,
+                  p + "self_attn.q_norm.weight": lw.q_norm,
+                  p + "self_attn.k_norm.weight": lw.k_norm,
+                  p + "mlp.gate_proj.weight": g, p + "mlp.up_proj.weight": u,
+                  p + "mlp.down_proj.weight": lw.w_down, p + "input_layernorm.weight": lw.ln1,
+                  p + "post_attention_layernorm.weight": lw.ln2})
+    save_file({k: x.contiguous() for k, x in t.items()}, str(tmp_path / "model.safetensors"))
+    with open(tmp_path / "config.json", "w") as f:
+        _json.dump(dict(vocab_size=512, hidden_size=256, intermediate_size=512,
+                        num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                        head_dim=128, rms_norm_eps=1e-6, rope_theta=1e6,
+                        tie_word_embeddings=False), f)
+    dev = torch.device("cuda", 0)
+    conf = dict(max_num_batched_tokens=128, max_num_seqs=2, num_blocks=32, block_size=16,
+                compat=False)
+    sp = SamplingParams(temperature=0, max_new_tokens=6, ignore_eos=True)
+    prompts = [[1, 2, 3, 4, 5], list(range(40, 77))]
+    a = Engine(Config(model=str(tmp_path), **conf), dev, max_slots=4).generate(prompts, sp)
+    b = Engine(Config(model="x", **conf), dev, model_config=cfg,
+               weights=Qwen3Weights(cfg, dev, seed=4, gen_device="cpu"),
+               max_slots=4).generate(prompts, sp)
+    assert a == b

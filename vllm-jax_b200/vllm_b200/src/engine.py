@@ -54,7 +54,25 @@ class Engine:
             device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
         torch.cuda.set_device(device)
         self.device = device
-        self.mcfg = model_config or get_config(config.model)
+        # config.model: a preset name (random-init weights of that architecture)
+        # or a local Hugging Face checkpoint directory (weights loaded, sharded)
+        hf_dir = config.model if os.path.isdir(config.model) else None
+        if model_config is not None:
+            self.mcfg = model_config
+        elif hf_dir:
+            from ..model.hf_loader import config_from_hf
+            self.mcfg = config_from_hf(hf_dir)
+        else:
+            self.mcfg = get_config(config.model)
+        if weights is None and hf_dir:
+            from ..model.hf_loader import load_hf_weights
+            weights = load_hf_weights(hf_dir, device, self.tp_rank, self.tp_size, self.mcfg)
+        if tokenizer is None and hf_dir and os.path.exists(
+                os.path.join(hf_dir, "tokenizer_config.json")):
+            from transformers import AutoTokenizer
+            self.tokenizer = tokenizer = AutoTokenizer.from_pretrained(hf_dir,
+                                                                       local_files_only=True)
+            self.eos_token_id = tokenizer.eos_token_id
         self.weights = weights or Qwen3Weights(self.mcfg, device, seed, self.tp_rank,
                                                self.tp_size)
         num_blocks = config.num_blocks
