@@ -102,3 +102,57 @@ def test_chunked_engine_greedy_vs_oracle():
         ulp = 2.0 ** (math.floor(math.log2(max(abs(top), 2.0 ** -10))) - 7)
         assert gap <= 4 * ulp + 1e-9, f"request {r} diverged at token {i}, oracle gap {gap}"
     assert n_match >= new * len(prompts) // 2
+
+
+def test_prefix_cached_engine_greedy_vs_oracle():
+    """Prompts sharing stems reuse cached KV blocks (written by earlier
+    requests, possibly after those finished); the oracle replays the recorded
+    schedule with the same block tables, so shared blocks hold the KV it
+    computed for the first request."""
+    from oracle.qwen3 import OracleQwen3, greedy_replay_chunked
+    from vllm_b200 import Config, SamplingParams
+    from vllm_b200.model.qwen3 import Qwen3Config, Qwen3Weights
+    from vllm_b200.src.engine import Engine
+    from vllm_b200.src.request import Request
+    cfg = Qwen3Config(vocab_size=4096, hidden_size=512, intermediate_size=1024,
+                      num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=4)
+    dev = torch.device("cuda", 0)
+    w = Qwen3Weights(cfg, dev, seed=9, gen_device="cpu")
+    nb, bs = 64, 16
+    Request.reset_ids()
+    eng = Engine(Config(model="tiny", max_num_batched_tokens=64, max_num_seqs=3,
+                        num_blocks=nb, block_size=bs, max_model_len=256,
+                        enable_chunked_prefill=True, enable_prefix_caching=True), dev,
+                 model_config=cfg, weights=w, max_slots=16)
+    eng.trace = []
+    rng = np.random.default_rng(3)
+    stem = rng.integers(0, cfg.vocab_size, 90).tolist()
+    prompts = [stem + rng.integers(0, cfg.vocab_size, n).tolist() for n in (5, 30, 1, 12, 40)]
+    prompts.append(stem[:64])                             # whole-block prefix of the stem
+    new = 8
+    outs = eng.generate(prompts, SamplingParams(temperature=0, max_new_tokens=new,
+                                                ignore_eos=True))
+    assert eng.scheduler.prefix_hit_tokens >= 4 * 80
+    assert [len(o) for o in outs] == [new] * len(prompts)
+    model = OracleQwen3(cfg, w.full_numpy(), nb, bs)
+    tokens, gaps = greedy_replay_chunked(model, eng.trace, prompts)
+    n_match, first = 0, None
+    for r, p in enumerate(prompts):
+        for i, (a, b) in enumerate(zip(outs[r], tokens[r][len(p):])):
+            if a != b:
+                first = (r, i) if first is None or i < first[1] else first
+                break
+            n_match += 1
+    print(f"prefix-cached greedy agreement {n_match}/{new * len(prompts)}; first {first}")
+    if first is not None:
+        r, i = first
+        k = -1
+        for g in gaps:
+            if r in g:
+                k += 1
+                if k == i:
+                    _, top, gap = g[r]
+                    break
+        ulp = 2.0 ** (math.floor(math.log2(max(abs(top), 2.0 ** -10))) - 7)
+        assert gap <= 4 * ulp + 1e-9, f"request {r} diverged at token {i}, oracle gap {gap}"
+    assert n_match >= new * len(prompts) // 2

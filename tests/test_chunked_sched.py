@@ -124,3 +124,112 @@ def test_chunked_scheduler_eos_and_determinism():
     a = _drive([200, 31, 77, 5], max_new=9, budget=48, max_seqs=3, num_blocks=20, bs=16, seed=5)
     b = _drive([200, 31, 77, 5], max_new=9, budget=48, max_seqs=3, num_blocks=20, bs=16, seed=5)
     assert a == b
+
+
+def _prefix_setup(num_blocks=40, budget=512):
+    from vllm_b200.config import Config
+    from vllm_b200.src.kv_cache_manager import KVCacheManager
+    from vllm_b200.src.request import Request
+    from vllm_b200.src.scheduler import ChunkedScheduler
+    Request.reset_ids()
+    cfg = Config(model="synthetic", max_num_batched_tokens=budget, max_num_seqs=8,
+                 num_blocks=num_blocks, block_size=16, compat=False,
+                 enable_chunked_prefill=True, enable_prefix_caching=True)
+    kv = KVCacheManager(num_blocks, 16)
+    return kv, ChunkedScheduler(cfg, kv)
+
+
+def _req(tokens, new=4):
+    from vllm_b200.sampling_params import SamplingParams
+    from vllm_b200.src.request import Request
+    return Request(tokens, SamplingParams(temperature=0, max_new_tokens=new, ignore_eos=True), -1)
+
+
+def _step(sched, tok=1):
+    batch = sched.schedule()
+    sampled = {}
+    for r, n in batch:
+        if r.num_computed_tokens + n == len(r):
+            r.token_ids.append(tok)
+            r.num_completion_tokens += 1
+            sampled[r.id] = tok
+    sched.postprocess(batch, sampled)
+    return batch
+
+
+def test_prefix_cache_shares_full_blocks_and_survives_finish():
+    kv, sched = _prefix_setup()
+    shared = list(range(1000, 1100))                       # 100 tokens: 6 full blocks
+    r1 = _req(shared + [1, 2, 3])
+    sched.add(r1)
+    _step(sched)                                           # r1 prefilled (103 tokens)
+    r2 = _req(shared + [7, 8])
+    sched.add(r2)
+    batch = _step(sched)
+    (_, n1), (b2, n2) = batch
+    assert b2 is r2 and n2 == 102 - 96                     # starts after 6 cached blocks
+    assert kv.block_ids(r2)[:6] == kv.block_ids(r1)[:6]
+    assert all(b.ref_count == 2 for b in kv.get_block_table(r1)[:6])
+    assert sched.prefix_hit_tokens == 96
+    while not sched.is_finished():
+        _step(sched)
+    assert len(kv.free_block_queue) == kv.num_blocks       # all released ...
+    assert len(kv.cached) >= 6                             # ... but still cached
+    r3 = _req(shared)                                      # exact prefix, 100 tokens
+    sched.add(r3)
+    batch = _step(sched)
+    assert batch[0][1] == 100 - 96 and sched.prefix_hit_tokens == 192
+
+
+def test_prefix_cache_never_skips_the_last_token_and_evicts_on_reuse():
+    kv, sched = _prefix_setup(num_blocks=12)
+    p = list(range(64))                                    # exactly 4 full blocks
+    r1 = _req(p, new=1)
+    sched.add(r1)
+    while not sched.is_finished():
+        _step(sched)
+    r2 = _req(p, new=1)
+    sched.add(r2)
+    batch = _step(sched)
+    assert batch[0][1] == 16                               # 3 blocks hit, last block recomputed
+    while not sched.is_finished():
+        _step(sched)
+    # a large unrelated prompt takes every free block: the cached ones are evicted
+    r3 = _req(list(range(5000, 5000 + 11 * 16 - 1)), new=1)
+    sched.add(r3)
+    _step(sched)
+    assert all(b.hash is None or kv.cached.get(b.hash) is b for b in kv.blocks)
+    hits = kv.lookup_prefix(_req(p), 10)
+    assert len(hits) < 3
+
+
+def test_prefix_cache_invariants_under_pressure():
+    """Random prompts drawn from a few shared stems on a small pool: budget and
+    seat caps hold, shared blocks are only full cached blocks, every request
+    completes and all blocks return to the free queue."""
+    kv, sched = _prefix_setup(num_blocks=48, budget=96)
+    rng = np.random.default_rng(4)
+    stems = [rng.integers(0, 1000, 70).tolist() for _ in range(3)]
+    reqs = []
+    for i in range(14):
+        tail = rng.integers(0, 1000, int(rng.integers(1, 40))).tolist()
+        r = _req(stems[i % 3][:int(rng.integers(10, 71))] + tail, new=int(rng.integers(1, 12)))
+        reqs.append(r)
+        sched.add(r)
+    steps = 0
+    while not sched.is_finished():
+        steps += 1
+        assert steps < 5000
+        batch = _step(sched)
+        assert sum(n for _, n in batch) <= 96
+        owners = {}
+        for r in sched.running:
+            for b in kv.get_block_table(r):
+                owners.setdefault(b.block_id, []).append(r)
+        for bid, rs in owners.items():
+            if len(rs) > 1:
+                b = kv.blocks[bid]
+                assert b.hash is not None and b.ref_count == len(rs)
+    assert all(r.num_completion_tokens == r.max_new_tokens for r in reqs)
+    assert len(kv.free_block_queue) == kv.num_blocks
+    assert sched.prefix_hit_tokens > 0

@@ -186,7 +186,8 @@ def test_engine_loads_a_local_hf_checkpoint(tmp_path):
                   p + "mlp.gate_proj.weight": g, p + "mlp.up_proj.weight": u,
                   p + "mlp.down_proj.weight": lw.w_down, p + "input_layernorm.weight": lw.ln1,
                   p + "post_attention_layernorm.weight": lw.ln2})
-    save_file({k: x.contiguous() for k, x in t.items()}, str(tmp_path / "model.safetensors"))
+    save_file({k: x.clone().contiguous() for k, x in t.items()},
+              str(tmp_path / "model.safetensors"))
     with open(tmp_path / "config.json", "w") as f:
         _json.dump(dict(vocab_size=512, hidden_size=256, intermediate_size=512,
                         num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,

@@ -23,6 +23,9 @@ class Config:
     # forward with decode rows (not in the reference). Implies compat=False
     # behaviour: position-addressed slots and blocks freed on finish.
     enable_chunked_prefill: bool = False
+    # Share the KV blocks of identical prompt prefixes between requests
+    # (needs enable_chunked_prefill: a request then starts after its hit).
+    enable_prefix_caching: bool = False
     # Under tensor parallelism: "nvlink" reduces decode-sized batches with the
     # fused peer-memory kernel (CUDA-graph capturable), "nccl" always uses
     # torch.distributed all-reduce (decode then runs eagerly).

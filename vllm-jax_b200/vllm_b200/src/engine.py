@@ -86,6 +86,8 @@ class Engine:
                                              group=process_group)
                 num_blocks = int(t.item())
             self.config = config = dataclasses.replace(config, num_blocks=num_blocks)
+        if config.enable_prefix_caching and not config.enable_chunked_prefill:
+            raise ValueError("enable_prefix_caching needs enable_chunked_prefill")
         if config.enable_chunked_prefill:
             if config.compat:
                 self.config = config = dataclasses.replace(config, compat=False)

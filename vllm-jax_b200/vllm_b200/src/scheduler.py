@@ -99,13 +99,20 @@ class ChunkedScheduler:
     known tokens plus a 1% watermark (their blocks are taken at admission). A request samples a token when a step processes
     its last known token. When the pool runs dry the request at the tail of
     `running` is preempted (blocks freed, recomputed from scratch later) unless
-    a shorter chunk still fits. Finished requests always release their blocks."""
+    a shorter chunk still fits. Finished requests always release their blocks.
+
+    With config.enable_prefix_caching, full blocks are published under a
+    chained hash of their tokens once computed; a new request shares the
+    cached blocks of its longest matching prefix and starts computing after
+    them (freed blocks keep their content until the FIFO reuses them)."""
 
     def __init__(self, config: Config, kv_cache_manager: KVCacheManager):
         self.max_num_batched_tokens = config.max_num_batched_tokens
         self.max_num_seqs = config.max_num_seqs
         self.kv_cache_manager = kv_cache_manager
         self.watermark_blocks = max(1, kv_cache_manager.num_blocks // 100)
+        self.prefix_caching = config.enable_prefix_caching
+        self.prefix_hit_tokens = 0
         self.waiting: deque[Request] = deque()
         self.running: deque[Request] = deque()
         self.finished_requests: list[Request] = []
@@ -152,17 +159,25 @@ class ChunkedScheduler:
             i += 1
         while self.waiting and len(out) < self.max_num_seqs and budget > 0:
             req = self.waiting[0]
+            # prefix cache: full blocks already holding this request's leading
+            # tokens are shared; at least the last token is computed (it samples)
+            hit = (kv.lookup_prefix(req, (len(req) - 1) // kv.block_size)
+                   if self.prefix_caching else [])
             # admission reserves blocks for every known token (its later chunks
             # never allocate) and keeps a watermark free for decode growth, so
             # that a new prompt does not immediately preempt running requests
-            need = -(-len(req) // kv.block_size)
-            if need + self.watermark_blocks > len(kv.free_block_queue):
+            need = -(-len(req) // kv.block_size) - len(hit)
+            free_hits = sum(1 for b in hit if b.ref_count == 0)
+            if need + self.watermark_blocks > len(kv.free_block_queue) - free_hits:
                 break
-            n = min(len(req), budget)
             self.waiting.popleft()
             req.status = Status.RUNNING
             self.running.append(req)
+            kv.acquire(req, hit)
+            req.num_computed_tokens = len(hit) * kv.block_size
+            self.prefix_hit_tokens += req.num_computed_tokens
             kv.grow(req, len(req))
+            n = min(len(req) - req.num_computed_tokens, budget)
             out.append((req, n))
             budget -= n
         return out
@@ -171,6 +186,8 @@ class ChunkedScheduler:
         """Advance computed tokens; finish requests whose sampled token ends them."""
         for req, n in batch:
             req.num_computed_tokens += n
+            if self.prefix_caching:
+                self.kv_cache_manager.register(req, req.num_computed_tokens)
             if req.id not in sampled:
                 continue
             token = sampled[req.id]
