@@ -280,11 +280,11 @@ VJ_API vj_status vj_sample(const void *logits, int64_t row_stride, int32_t num_r
 #define VJ_TP_MAX_RANKS 8
 #define VJ_IPC_HANDLE_BYTES 64
 
-/* Grid of vj_allreduce_add_rmsnorm on this device (2 x SMs); every rank must
+/* Grid of vj_allreduce_add_rmsnorm on this device (4 CTAs per SM); every rank must
  * report the same value. */
 VJ_API int32_t vj_tp_grid(void);
 /* Bytes of the flag region at the start of a rank's communication memory:
- * flags [world][grid] u32, epochs [grid] u32, one error word. */
+ * flags [2][world][grid] u32, epochs [grid] u32, one error word. */
 VJ_API size_t vj_tp_flags_bytes(int32_t world);
 /* cudaMalloc'd, zeroed device memory that can be shared with
  * vj_ipc_get_handle (a torch caching-allocator block cannot). */
@@ -297,18 +297,21 @@ VJ_API vj_status vj_ipc_open_handle(const void *handle, void **ptr);
 VJ_API vj_status vj_ipc_close_handle(void *ptr);
 
 /* out = residual + sum over ranks of bufs[r][rows, hidden] (fp32 sum in rank
- * order, rounded to bf16, added in bf16); y = RMSNorm(out) * weight as
- * vj_add_rmsnorm. bufs[r] is rank r's partial (peer pointers, own included);
- * peer_flags[r] the flag region of rank r; flags this rank's own. Each CTA
+ * order, rounded to bf16, added in bf16) -> residual_out; y = RMSNorm(out) *
+ * weight as vj_add_rmsnorm. bufs[r] is rank r's partial (peer pointers, own
+ * included); peer_flags[r] the flag region of rank r; flags this rank's own.
+ * results == NULL: one-shot (every rank reads every partial). Otherwise
+ * results[r] is rank r's result buffer ([rows, hidden], peer pointers) and the
+ * reduction is two-shot (reduce a slice, then gather the slices). Each CTA
  * signals its counterpart on every peer and waits for theirs (bounded: 2 s;
  * on timeout the error word of `flags` is set and the CTA returns). All ranks
  * must make the same sequence of calls; a buffer may be rewritten only after
- * the next call on it has been made by every rank (use two buffers in
- * alternation). residual / residual_out may be NULL. */
+ * the next call has been made by every rank (use two sets in alternation).
+ * residual may be NULL (out = the sum). */
 VJ_API vj_status vj_allreduce_add_rmsnorm(
-    const void *const *bufs, uint32_t *const *peer_flags, uint32_t *flags, int32_t rank,
-    int32_t world, const void *residual, const void *weight, void *residual_out, void *y,
-    int64_t rows, int32_t hidden, float eps, cudaStream_t stream);
+    const void *const *bufs, void *const *results, uint32_t *const *peer_flags,
+    uint32_t *flags, int32_t rank, int32_t world, const void *residual, const void *weight,
+    void *residual_out, void *y, int64_t rows, int32_t hidden, float eps, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

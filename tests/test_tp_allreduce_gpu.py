@@ -41,7 +41,7 @@ def test_fused_allreduce_matches_sum_then_add_rmsnorm(world, rows, hidden):
     for (base, fb, bb), pt in zip(regions, parts):
         device_view(base + fb + site * bb, (rows, hidden), torch.bfloat16, dev).copy_(pt)
         # flags this rank waits on: already far past any epoch
-        device_view(base, (world * G,), torch.int32, dev).fill_(1 << 30)
+        device_view(base, (2 * world * G,), torch.int32, dev).fill_(1 << 30)
     s = torch.zeros(rows, hidden, dtype=torch.float32, device=dev)
     for pt in parts:
         s += pt.float()
@@ -51,12 +51,12 @@ def test_fused_allreduce_matches_sum_then_add_rmsnorm(world, rows, hidden):
     for rank in range(world):
         x_out = torch.empty_like(x)
         y = torch.empty_like(x)
-        _native.call("vj_allreduce_add_rmsnorm", ctypes.cast(bufs, ctypes.c_void_p),
+        _native.call("vj_allreduce_add_rmsnorm", ctypes.cast(bufs, ctypes.c_void_p), None,
                      ctypes.cast(flags, ctypes.c_void_p), ctypes.c_void_p(regions[rank][0]),
                      rank, world, x.data_ptr(), w.data_ptr(), x_out.data_ptr(), y.data_ptr(),
                      rows, hidden, 1e-6, torch.cuda.current_stream().cuda_stream)
         torch.cuda.synchronize()
-        err = device_view(regions[rank][0] + (world + 1) * G * 4, (1,), torch.int32, dev)
+        err = device_view(regions[rank][0] + (2 * world + 1) * G * 4, (1,), torch.int32, dev)
         assert int(err.item()) == 0
         assert torch.equal(x_out, ref_x), f"rank {rank}: residual differs"
         assert torch.equal(y, ref_y), f"rank {rank}: normed output differs"
@@ -68,11 +68,11 @@ def test_fused_allreduce_rejects_bad_arguments():
     from vllm_b200 import _native
     lib = _native.load()
     null = (ctypes.c_void_p * 2)(None, None)
-    st = lib.vj_allreduce_add_rmsnorm(ctypes.cast(null, ctypes.c_void_p),
+    st = lib.vj_allreduce_add_rmsnorm(ctypes.cast(null, ctypes.c_void_p), None,
                                       ctypes.cast(null, ctypes.c_void_p), None, 0, 9, None,
                                       None, None, None, 4, 1024, 1e-6, None)
     assert st == _native.VJ_ERR_INVALID_ARGUMENT
-    st = lib.vj_allreduce_add_rmsnorm(ctypes.cast(null, ctypes.c_void_p),
+    st = lib.vj_allreduce_add_rmsnorm(ctypes.cast(null, ctypes.c_void_p), None,
                                       ctypes.cast(null, ctypes.c_void_p), None, 0, 2, None,
                                       None, None, None, 4, 10000, 1e-6, None)
     assert st == _native.VJ_ERR_UNSUPPORTED

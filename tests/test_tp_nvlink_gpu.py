@@ -1,8 +1,9 @@
 """Tensor parallelism over NVLink on 2 GPUs (skipped with fewer).
 
-Two processes (one per GPU, NCCL for setup only) build a TPComm and run the
-fused all-reduce + add + RMSNorm many times, alternating the two buffers, in
-eager mode and replayed from a CUDA graph; every result must equal, bit for
+Two processes (one per GPU, NCCL for setup only) build a TPComm (one-shot,
+then two-shot) and run the fused all-reduce + add + RMSNorm many times,
+alternating the two buffers, in eager mode and replayed from a CUDA graph;
+every result must equal, bit for
 bit, the fp32 rank-order sum of the partials (gathered with NCCL) followed
 by vj_add_rmsnorm. Then a 2-rank Engine with the NVLink path generates with
 CUDA-graph decode and must agree with the NCCL path on the first tokens.
@@ -26,6 +27,65 @@ def _free_port():
         return s.getsockname()[1]
 
 
+def _check_comm(comm, rank, world, dev, H):
+    import torch.distributed as dist
+
+    from vllm_b200.kernels.fused import add_rmsnorm
+    g = torch.Generator(device="cpu").manual_seed(1234)
+    w = (1 + 0.1 * torch.randn(H, generator=g)).bfloat16().to(dev)
+
+    def reference(part, x):
+        parts = [torch.empty_like(part) for _ in range(world)]
+        dist.all_gather(parts, part)
+        s = torch.zeros(part.shape, dtype=torch.float32, device=dev)
+        for p in parts:
+            s += p.float()
+        return add_rmsnorm(s.bfloat16(), w, 1e-6, residual=x)
+
+    gl = torch.Generator(device="cpu").manual_seed(77 + rank)
+    for it in range(24):
+        T = [1, 7, 64, 96][it % 4]
+        site = it % 2
+        part = torch.randn(T, H, generator=gl).bfloat16().to(dev)
+        x = torch.randn(T, H, generator=torch.Generator().manual_seed(it)).bfloat16().to(dev)
+        comm.buffer(site, T).copy_(part)
+        xo, y = comm.allreduce_add_rmsnorm(site, T, x, w, 1e-6)
+        rx, ry = reference(part, x)
+        assert torch.equal(xo, rx) and torch.equal(y, ry), f"eager call {it} differs"
+    # CUDA graph of four calls (both buffers twice), replayed with new inputs
+    T = 32
+    src = [torch.zeros(T, H, dtype=torch.bfloat16, device=dev) for _ in range(4)]
+    xin = torch.zeros(T, H, dtype=torch.bfloat16, device=dev)
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            cur = xin
+            outs = []
+            for k in range(4):
+                comm.buffer(k % 2, T).copy_(src[k])
+                cur, y = comm.allreduce_add_rmsnorm(k % 2, T, cur, w, 1e-6)
+                outs.append((cur, y))
+    torch.cuda.current_stream(dev).wait_stream(s)
+    for rep in range(3):
+        for k in range(4):
+            src[k].copy_(torch.randn(T, H, generator=gl).bfloat16())
+        xin.copy_(torch.randn(T, H, generator=torch.Generator().manual_seed(900 + rep))
+                  .bfloat16())
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        cur = xin.clone()
+        for k in range(4):
+            rx, ry = reference(src[k], cur)
+            assert torch.equal(outs[k][0], rx) and torch.equal(outs[k][1], ry), \
+                f"graph replay {rep} call {k} differs"
+            cur = rx
+    assert not comm.failed()
+    del graph
+    comm.close()
+
+
 def _worker(rank, world, port, q):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -37,63 +97,12 @@ def _worker(rank, world, port, q):
         dev = torch.device("cuda", rank)
         dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                                 timeout=datetime.timedelta(seconds=60))
-        from vllm_b200.kernels.fused import add_rmsnorm
         from vllm_b200.src.tp_comm import TPComm
         H, R = 2048, 96
-        comm = TPComm(dist.group.WORLD, rank, world, dev, R, H)
-        g = torch.Generator(device="cpu").manual_seed(1234)
-        w = (1 + 0.1 * torch.randn(H, generator=g)).bfloat16().to(dev)
+        for two_shot in (False, True):
+            _check_comm(TPComm(dist.group.WORLD, rank, world, dev, R, H, two_shot=two_shot),
+                        rank, world, dev, H)
 
-        def reference(part, x):
-            parts = [torch.empty_like(part) for _ in range(world)]
-            dist.all_gather(parts, part)
-            s = torch.zeros(part.shape, dtype=torch.float32, device=dev)
-            for p in parts:
-                s += p.float()
-            return add_rmsnorm(s.bfloat16(), w, 1e-6, residual=x)
-
-        gl = torch.Generator(device="cpu").manual_seed(77 + rank)
-        for it in range(24):
-            T = [1, 7, 64, 96][it % 4]
-            site = it % 2
-            part = torch.randn(T, H, generator=gl).bfloat16().to(dev)
-            x = torch.randn(T, H, generator=torch.Generator().manual_seed(it)).bfloat16().to(dev)
-            comm.buffer(site, T).copy_(part)
-            xo, y = comm.allreduce_add_rmsnorm(site, T, x, w, 1e-6)
-            rx, ry = reference(part, x)
-            assert torch.equal(xo, rx) and torch.equal(y, ry), f"eager call {it} differs"
-        # CUDA graph of four calls (both buffers twice), replayed with new inputs
-        T = 32
-        src = [torch.zeros(T, H, dtype=torch.bfloat16, device=dev) for _ in range(4)]
-        xin = torch.zeros(T, H, dtype=torch.bfloat16, device=dev)
-        s = torch.cuda.Stream(dev)
-        s.wait_stream(torch.cuda.current_stream(dev))
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(s):
-            with torch.cuda.graph(graph, stream=s):
-                cur = xin
-                outs = []
-                for k in range(4):
-                    comm.buffer(k % 2, T).copy_(src[k])
-                    cur, y = comm.allreduce_add_rmsnorm(k % 2, T, cur, w, 1e-6)
-                    outs.append((cur, y))
-        torch.cuda.current_stream(dev).wait_stream(s)
-        for rep in range(3):
-            for k in range(4):
-                src[k].copy_(torch.randn(T, H, generator=gl).bfloat16())
-            xin.copy_(torch.randn(T, H, generator=torch.Generator().manual_seed(900 + rep))
-                      .bfloat16())
-            graph.replay()
-            torch.cuda.synchronize(dev)
-            cur = xin.clone()
-            for k in range(4):
-                rx, ry = reference(src[k], cur)
-                assert torch.equal(outs[k][0], rx) and torch.equal(outs[k][1], ry), \
-                    f"graph replay {rep} call {k} differs"
-                cur = rx
-        assert not comm.failed()
-        del graph
-        comm.close()
         # engine: NVLink path (CUDA-graph decode) vs NCCL path (eager)
         from vllm_b200 import Config, SamplingParams
         from vllm_b200.model.qwen3 import Qwen3Config, Qwen3Weights

@@ -4,22 +4,24 @@
 // with the weights split by KV head the row-parallel GEMM outputs must be
 // summed over ranks before `attn_output += x; norm`).
 //
-// One-shot over NVLink peer memory: every rank's GEMM writes its partial
-// [rows, hidden] into its own communication buffer (cudaIpc-shared); then
-// each CTA of this kernel
-//   1. announces "my partial is ready" to its counterpart CTA on every peer
-//      (st.release.sys of a per-CTA epoch into the peer's flag array) and
-//      waits, bounded by time and iterations, until every peer's counterpart
-//      has announced the same epoch;
-//   2. for its rows: loads the partial row of every rank (plain peer loads,
-//      16 B per lane, no multicast), sums them in fp32 in rank order (so all
-//      ranks get bit-identical results), rounds to bf16, adds the residual in
-//      bf16, and applies RMSNorm exactly as vj_add_rmsnorm does;
-//   3. writes the new residual and the normed row locally.
+// Over NVLink peer memory: every rank's GEMM writes its partial [rows,
+// hidden] into its own communication buffer (cudaIpc-shared). Each CTA of
+// this kernel then announces "my partial is ready" to its counterpart CTA on
+// every peer (st.release.sys of a per-CTA epoch into the peer's flag array)
+// and waits, bounded by time and iterations, for theirs. A CTA works on one
+// row at a time, 16 bytes per thread, with the loads of all ranks in flight
+// together (plain peer loads through L2, no multicast); partials are summed
+// in fp32 in rank order, so every rank gets bit-identical results, rounded to
+// bf16, added to the residual in bf16, and normalised as vj_add_rmsnorm does.
+//   one-shot (2 ranks): every rank reduces every row.
+//   two-shot (more ranks): rank r reduces rows [r*S, (r+1)*S) into its result
+//     buffer, a second CTA barrier, then every rank gathers the other slices
+//     (CTA b of rank p produced exactly the rows CTA b reads from it), so each
+//     rank moves 2 (N-1)/N of the data over NVLink instead of (N-1).
 // The kernel never waits for a peer's kernel to FINISH; buffers alternate
 // between two parities, and arriving at call i+1 proves a peer finished
 // call i, so a buffer is rewritten only after every peer stopped reading it.
-// The grid is fixed (2 x SMs), each CTA keeps its own epoch counter, so the
+// The grid is fixed (4 CTAs per SM), each CTA keeps its own epoch counter, so the
 // same launch can be captured in a CUDA graph and replayed.
 #include "../../include/vjattn.h"
 #include "vj_common.cuh"
@@ -31,18 +33,20 @@ namespace vj {
 namespace {
 
 constexpr int kArThreads = 256;
-constexpr int kArMaxVec = 4;        // hidden <= 8192
+constexpr int kArCtasPerSm = 4;   // one row per CTA for decode batches up to 4 x SMs
+constexpr int kArMaxVec = 4;        // hidden <= 8 * 256 * 4 = 8192
 constexpr uint64_t kArSpinLimit = 1ull << 26;
 
 struct ArArgs {
   const __nv_bfloat16 *bufs[VJ_TP_MAX_RANKS];  // partial of each rank (own included)
-  uint32_t *peer_flags[VJ_TP_MAX_RANKS];       // flag array in each rank's memory
-  uint32_t *flags;                              // mine: [world][grid]
+  __nv_bfloat16 *results[VJ_TP_MAX_RANKS];     // two-shot: reduced slice of each rank
+  uint32_t *peer_flags[VJ_TP_MAX_RANKS];       // flag region in each rank's memory
+  uint32_t *flags;                              // mine: [2][world][grid]
   uint32_t *epochs;                             // mine: [grid]
   int32_t *error;
   const __nv_bfloat16 *residual, *weight;
   __nv_bfloat16 *residual_out, *y;
-  int rank, world, rows, hidden;
+  int rank, world, rows, hidden, two_shot;
   float eps;
 };
 
@@ -54,19 +58,162 @@ VJ_DEV uint32_t ld_acquire_sys(const uint32_t *p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-VJ_DEV uint4 ld_peer16(const void *p) {
-  uint4 v;
-  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
+
+// Cross-rank barrier between counterpart CTAs: announce `epoch` in every
+// peer's flag slot (rank, b) of flag set `set`, wait (bounded) for every
+// peer's announcement in mine. The release is cumulative over the CTA's
+// writes that precede the __syncthreads.
+VJ_DEV bool cta_barrier(const ArArgs &a, int set, uint32_t epoch, int *s_fail) {
+  const int b = blockIdx.x, G = gridDim.x, tid = threadIdx.x;
+  const size_t base = (size_t)set * a.world * G;
+  __syncthreads();
+  if (tid < a.world && tid != a.rank) {
+    st_release_sys(a.peer_flags[tid] + base + (size_t)a.rank * G + b, epoch);
+    const uint32_t *f = a.flags + base + (size_t)tid * G + b;
+    const uint64_t t0 = globaltimer_ns();
+    uint64_t it = 0;
+    while ((int32_t)(ld_acquire_sys(f) - epoch) < 0) {
+      if (++it > kArSpinLimit || globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicExch(a.error, 1);
+        *s_fail = 1;
+        break;
+      }
+      if (it > 4096) __nanosleep(64);
+    }
+  }
+  __syncthreads();
+  return *s_fail == 0;
 }
 
-__global__ void __launch_bounds__(kArThreads)
+// Sum over the block of one double per thread; every thread gets the total.
+VJ_DEV double block_sum(double v, double *red) {
+  const int tid = threadIdx.x;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((tid & 31) == 0) red[tid >> 5] = v;
+  __syncthreads();
+  double t = 0.0;
+#pragma unroll
+  for (int w = 0; w < kArThreads / 32; ++w) t += red[w];
+  __syncthreads();   // red[] is rewritten by the next row
+  return t;
+}
+
+VJ_DEV double sq8(const uint32_t o[4]) {
+  double ss = 0.0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const double lo = bf16_lo(o[j]), hi = bf16_hi(o[j]);
+    ss += lo * lo + hi * hi;
+  }
+  return ss;
+}
+
+// x = residual + bf16(fp32 sum over ranks, rank order) of `row`; written to
+// residual_out (and to `res`, the two-shot result buffer). Returns 1/rms.
+VJ_DEV float reduce_row(const ArArgs &a, int row, __nv_bfloat16 *res, double *red) {
+  const int H = a.hidden, nvec = H / 8, tid = threadIdx.x;
+  const size_t off = (size_t)row * H;
+  double ss = 0.0;
+#pragma unroll
+  for (int k = 0; k < kArMaxVec; ++k) {
+    const int i = tid + k * kArThreads;
+    if (i < nvec) {
+      uint4 v[VJ_TP_MAX_RANKS];
+#pragma unroll
+      for (int r = 0; r < VJ_TP_MAX_RANKS; ++r) {
+        // published by the peer's release, acquired in cta_barrier; read
+        // through L2 (ld.global.cg), never from a possibly stale L1 line
+        if (r < a.world) v[r] = __ldcg(reinterpret_cast<const uint4 *>(a.bufs[r] + off) + i);
+      }
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+      for (int r = 0; r < VJ_TP_MAX_RANKS; ++r) {
+        if (r < a.world) {
+          const uint32_t w[4] = {v[r].x, v[r].y, v[r].z, v[r].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            acc[2 * j] += bf16_lo(w[j]);
+            acc[2 * j + 1] += bf16_hi(w[j]);
+          }
+        }
+      }
+      uint32_t o[4];
+      if (a.residual) {
+        const uint4 xr = __ldg(reinterpret_cast<const uint4 *>(a.residual + off) + i);
+        const uint32_t xw[4] = {xr.x, xr.y, xr.z, xr.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          // bf16(sum) + x in bf16, as the reference's `attn_output += x`
+          o[j] = pack_bf16(round_bf16(acc[2 * j]) + bf16_lo(xw[j]),
+                           round_bf16(acc[2 * j + 1]) + bf16_hi(xw[j]));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = pack_bf16(acc[2 * j], acc[2 * j + 1]);
+      }
+      const uint4 xv = make_uint4(o[0], o[1], o[2], o[3]);
+      reinterpret_cast<uint4 *>(a.residual_out + off)[i] = xv;
+      if (res) reinterpret_cast<uint4 *>(res + off)[i] = xv;
+      ss += sq8(o);
+    }
+  }
+  const double tot = block_sum(ss, red);
+  const float ms = __fdiv_rn(static_cast<float>(tot), static_cast<float>(H));
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
+}
+
+// Two-shot gather: copy `row` of x from a peer's result buffer. Returns 1/rms.
+VJ_DEV float gather_row(const ArArgs &a, int row, const __nv_bfloat16 *src, double *red) {
+  const int H = a.hidden, nvec = H / 8, tid = threadIdx.x;
+  const size_t off = (size_t)row * H;
+  double ss = 0.0;
+#pragma unroll
+  for (int k = 0; k < kArMaxVec; ++k) {
+    const int i = tid + k * kArThreads;
+    if (i < nvec) {
+      const uint4 xv = __ldcg(reinterpret_cast<const uint4 *>(src + off) + i);
+      reinterpret_cast<uint4 *>(a.residual_out + off)[i] = xv;
+      const uint32_t o[4] = {xv.x, xv.y, xv.z, xv.w};
+      ss += sq8(o);
+    }
+  }
+  const double tot = block_sum(ss, red);
+  const float ms = __fdiv_rn(static_cast<float>(tot), static_cast<float>(H));
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
+}
+
+// y = bf16(x * (inv * w)) of `row`; x re-read from residual_out, where this
+// same thread wrote it.
+VJ_DEV void norm_row(const ArArgs &a, int row, float inv) {
+  const int H = a.hidden, nvec = H / 8, tid = threadIdx.x;
+  const size_t off = (size_t)row * H;
+#pragma unroll
+  for (int k = 0; k < kArMaxVec; ++k) {
+    const int i = tid + k * kArThreads;
+    if (i < nvec) {
+      const uint4 xv = reinterpret_cast<const uint4 *>(a.residual_out + off)[i];
+      const uint4 ww = __ldg(reinterpret_cast<const uint4 *>(a.weight) + i);
+      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, wws[4] = {ww.x, ww.y, ww.z, ww.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float m0 = __fmul_rn(inv, bf16_lo(wws[j])), m1 = __fmul_rn(inv, bf16_hi(wws[j]));
+        o[j] = pack_bf16(__fmul_rn(bf16_lo(xw[j]), m0), __fmul_rn(bf16_hi(xw[j]), m1));
+      }
+      reinterpret_cast<uint4 *>(a.y + off)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kArThreads, kArCtasPerSm)
 allreduce_add_rmsnorm_kernel(ArArgs a) {
   const int b = blockIdx.x, G = gridDim.x, tid = threadIdx.x;
   __shared__ uint32_t s_epoch;
   __shared__ int s_fail;
+  __shared__ double red[kArThreads / 32];
   if (tid == 0) {
     s_epoch = a.epochs[b] + 1;
     a.epochs[b] = s_epoch;
@@ -74,114 +221,39 @@ allreduce_add_rmsnorm_kernel(ArArgs a) {
   }
   __syncthreads();
   const uint32_t epoch = s_epoch;
-  // 1. announce, then wait for every peer's counterpart CTA
-  if (tid < a.world && tid != a.rank) {
-    __threadfence_system();
-    st_release_sys(a.peer_flags[tid] + (size_t)a.rank * G + b, epoch);
-    const uint32_t *f = a.flags + (size_t)tid * G + b;
-    const uint64_t t0 = globaltimer_ns();
-    uint64_t it = 0;
-    while ((int32_t)(ld_acquire_sys(f) - epoch) < 0) {
-      if (++it > kArSpinLimit || globaltimer_ns() - t0 > kWaitLimitNs) {
-        atomicExch(a.error, 1);
-        s_fail = 1;
-        break;
-      }
-      __nanosleep(32);
-    }
+  // 1. every peer's partial is ready
+  if (!cta_barrier(a, 0, epoch, &s_fail)) return;
+  if (!a.two_shot) {
+    // one-shot: every rank reduces every row
+    for (int row = b; row < a.rows; row += G) norm_row(a, row, reduce_row(a, row, nullptr, red));
+    return;
   }
-  __syncthreads();
-  if (s_fail) return;
-
-  // 2-3. rows b, b + G, ...
-  const int H = a.hidden, nvec = H / 8;
-  __shared__ double red[kArThreads / 32];
-  for (int row = b; row < a.rows; row += G) {
-    const size_t off = (size_t)row * H;
-    uint4 keep[kArMaxVec];
-    double ss = 0.0;
-#pragma unroll
-    for (int k = 0; k < kArMaxVec; ++k) {
-      const int i = tid + k * kArThreads;
-      if (i < nvec) {
-        float acc[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-        for (int r = 0; r < a.world; ++r) {
-          const uint4 v = ld_peer16(a.bufs[r] + off + 8 * i);
-          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            acc[2 * j] += bf16_lo(w[j]);
-            acc[2 * j + 1] += bf16_hi(w[j]);
-          }
-        }
-        uint32_t o[4];
-        if (a.residual) {
-          const uint4 xr = *reinterpret_cast<const uint4 *>(a.residual + off + 8 * i);
-          const uint32_t xw[4] = {xr.x, xr.y, xr.z, xr.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            // bf16(sum) + x in bf16, as the reference's `attn_output += x`
-            o[j] = pack_bf16(round_bf16(acc[2 * j]) + bf16_lo(xw[j]),
-                             round_bf16(acc[2 * j + 1]) + bf16_hi(xw[j]));
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) o[j] = pack_bf16(acc[2 * j], acc[2 * j + 1]);
-        }
-        const uint4 rv = make_uint4(o[0], o[1], o[2], o[3]);
-        if (a.residual_out) *reinterpret_cast<uint4 *>(a.residual_out + off + 8 * i) = rv;
-        keep[k] = rv;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const double lo = bf16_lo(o[j]), hi = bf16_hi(o[j]);
-          ss += lo * lo + hi * hi;
-        }
-      }
-    }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if ((tid & 31) == 0) red[tid >> 5] = ss;
-    __syncthreads();
-    if (tid < 32) {
-      double v = tid < kArThreads / 32 ? red[tid] : 0.0;
-#pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (tid == 0) red[0] = v;
-    }
-    __syncthreads();
-    const float ms = __fdiv_rn(static_cast<float>(red[0]), static_cast<float>(H));
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
-    __syncthreads();   // red[] is rewritten by the next row
-#pragma unroll
-    for (int k = 0; k < kArMaxVec; ++k) {
-      const int i = tid + k * kArThreads;
-      if (i < nvec) {
-        const uint4 xv = keep[k];
-        const uint4 ww = __ldg(reinterpret_cast<const uint4 *>(a.weight) + i);
-        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, wws[4] = {ww.x, ww.y, ww.z, ww.w};
-        uint32_t o[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float m0 = __fmul_rn(inv, bf16_lo(wws[j])), m1 = __fmul_rn(inv, bf16_hi(wws[j]));
-          o[j] = pack_bf16(__fmul_rn(bf16_lo(xw[j]), m0), __fmul_rn(bf16_hi(xw[j]), m1));
-        }
-        *reinterpret_cast<uint4 *>(a.y + off + 8 * i) = make_uint4(o[0], o[1], o[2], o[3]);
-      }
-    }
+  // two-shot: rank r reduces rows [r*S, (r+1)*S) into its result buffer ...
+  const int S = (a.rows + a.world - 1) / a.world;
+  const int lo = a.rank * S, hi = min(a.rows, lo + S);
+  for (int row = lo + b; row < hi; row += G) {
+    norm_row(a, row, reduce_row(a, row, a.results[a.rank], red));
+  }
+  // ... 2. every peer's slice is reduced (CTA b of rank p wrote exactly the
+  // rows CTA b reads from it) ...
+  if (!cta_barrier(a, 1, epoch, &s_fail)) return;
+  // ... 3. and gathers the other slices
+  for (int p = 0; p < a.world; ++p) {
+    if (p == a.rank) continue;
+    const int plo = p * S, phi = min(a.rows, plo + S);
+    for (int row = plo + b; row < phi; row += G) norm_row(a, row, gather_row(a, row, a.results[p], red));
   }
 }
 
 }  // namespace
 }  // namespace vj
 
-extern "C" int32_t vj_tp_grid(void) { return 2 * vj::num_sms(); }
+extern "C" int32_t vj_tp_grid(void) { return vj::kArCtasPerSm * vj::num_sms(); }
 
 extern "C" size_t vj_tp_flags_bytes(int32_t world) {
-  // flags [world][grid] + epochs [grid] + error word, rounded to 4 KB
+  // flags [2][world][grid] + epochs [grid] + error word, rounded to 4 KB
   const size_t g = (size_t)vj_tp_grid();
-  const size_t n = (g * (size_t)(world + 1) + 1) * sizeof(uint32_t);
+  const size_t n = (g * (size_t)(2 * world + 1) + 1) * sizeof(uint32_t);
   return (n + 4095) & ~(size_t)4095;
 }
 
@@ -241,35 +313,37 @@ extern "C" vj_status vj_ipc_close_handle(void *ptr) {
 }
 
 extern "C" vj_status vj_allreduce_add_rmsnorm(
-    const void *const *bufs, uint32_t *const *peer_flags, uint32_t *flags, int32_t rank,
-    int32_t world, const void *residual, const void *weight, void *residual_out, void *y,
-    int64_t rows, int32_t hidden, float eps, cudaStream_t stream) {
+    const void *const *bufs, void *const *results, uint32_t *const *peer_flags, uint32_t *flags,
+    int32_t rank, int32_t world, const void *residual, const void *weight, void *residual_out,
+    void *y, int64_t rows, int32_t hidden, float eps, cudaStream_t stream) {
   using namespace vj;
   if (world < 1 || world > VJ_TP_MAX_RANKS || rank < 0 || rank >= world) {
     return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_allreduce_add_rmsnorm: bad rank/world");
   }
-  if (rows < 0 || rows > INT32_MAX || hidden <= 0 || hidden % 8 || hidden > 8 * kArThreads * kArMaxVec) {
+  if (rows < 0 || rows > INT32_MAX || hidden <= 0 || hidden % 8 ||
+      hidden > 8 * kArThreads * kArMaxVec) {
     return set_error(VJ_ERR_UNSUPPORTED,
                      "vj_allreduce_add_rmsnorm: hidden must be a multiple of 8, <= 8192");
   }
-  if (!bufs || !peer_flags || !flags || !weight || !y) {
+  if (!bufs || !peer_flags || !flags || !weight || !y || !residual_out) {
     return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_allreduce_add_rmsnorm: null pointer");
   }
   ArArgs a{};
   for (int r = 0; r < world; ++r) {
-    if (!bufs[r] || (r != rank && !peer_flags[r])) {
+    if (!bufs[r] || (r != rank && !peer_flags[r]) || (results && !results[r])) {
       return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_allreduce_add_rmsnorm: null peer pointer");
     }
-    if (reinterpret_cast<uintptr_t>(bufs[r]) & 15u) {
+    if ((reinterpret_cast<uintptr_t>(bufs[r]) | (results ? reinterpret_cast<uintptr_t>(results[r]) : 0)) & 15u) {
       return set_error(VJ_ERR_UNSUPPORTED, "vj_allreduce_add_rmsnorm: buffers must be 16-byte aligned");
     }
     a.bufs[r] = static_cast<const __nv_bfloat16 *>(bufs[r]);
+    a.results[r] = results ? static_cast<__nv_bfloat16 *>(results[r]) : nullptr;
     a.peer_flags[r] = peer_flags[r];
   }
   const int G = vj_tp_grid();
   a.flags = flags;
-  a.epochs = flags + (size_t)world * G;
-  a.error = reinterpret_cast<int32_t *>(flags + (size_t)(world + 1) * G);
+  a.epochs = flags + (size_t)2 * world * G;
+  a.error = reinterpret_cast<int32_t *>(flags + (size_t)(2 * world + 1) * G);
   a.residual = static_cast<const __nv_bfloat16 *>(residual);
   a.weight = static_cast<const __nv_bfloat16 *>(weight);
   a.residual_out = static_cast<__nv_bfloat16 *>(residual_out);
@@ -278,6 +352,7 @@ extern "C" vj_status vj_allreduce_add_rmsnorm(
   a.world = world;
   a.rows = (int)rows;
   a.hidden = hidden;
+  a.two_shot = results != nullptr && world > 1;
   a.eps = eps;
   // every call launches the same grid, even with no rows: the per-CTA epochs
   // and the peers' waits must advance together on all ranks

@@ -66,8 +66,8 @@ PROTOTYPES: dict[str, tuple] = {
     "vj_ipc_get_handle": (c_int, [c_vp, c_vp]),
     "vj_ipc_open_handle": (c_int, [c_vp, c_vp]),
     "vj_ipc_close_handle": (c_int, [c_vp]),
-    "vj_allreduce_add_rmsnorm": (c_int, [c_vp, c_vp, c_vp, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp,
-                                         c_i64, c_i32, ctypes.c_float, c_vp]),
+    "vj_allreduce_add_rmsnorm": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_vp, c_vp, c_vp,
+                                         c_vp, c_i64, c_i32, ctypes.c_float, c_vp]),
     "vj_sample": (c_int, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                           c_i32, c_vp, c_vp, c_vp]),
 }

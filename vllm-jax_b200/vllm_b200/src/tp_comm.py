@@ -1,7 +1,8 @@
 """NVLink peer-memory communicator for tensor parallelism.
 
 Each rank allocates one communication region (vj_comm_alloc: flags, then two
-partial buffers of [max_rows, hidden] bf16), exports it with cudaIpc, and maps
+partial buffers of [max_rows, hidden] bf16, and for the two-shot reduction
+two result buffers), exports it with cudaIpc, and maps
 every peer's region (handles exchanged once with all_gather_object). The
 model's row-parallel GEMMs (o_proj, down_proj) write their partial products
 straight into buffer `site` (0 for o_proj, 1 for down_proj, so consecutive
@@ -41,17 +42,21 @@ def device_view(ptr: int, shape: tuple, dtype: torch.dtype, device: torch.device
 class TPComm:
 
     def __init__(self, group, rank: int, world: int, device: torch.device, max_rows: int,
-                 hidden: int):
+                 hidden: int, two_shot: bool | None = None):
         if world > 8:
             raise ValueError("at most 8 ranks")
         self.rank, self.world, self.device = rank, world, device
         self.max_rows, self.hidden = max_rows, hidden
         self.group = group
+        # one-shot moves (N-1) x the data per rank, two-shot 2 (N-1)/N x plus a
+        # second barrier: two-shot from 4 ranks on
+        self.two_shot = world > 2 if two_shot is None else bool(two_shot)
         lib = _native.load()
         self.grid = int(lib.vj_tp_grid())
         self.flag_bytes = int(lib.vj_tp_flags_bytes(world))
         self.buf_bytes = (max_rows * hidden * 2 + 4095) // 4096 * 4096
-        total = self.flag_bytes + 2 * self.buf_bytes
+        nbuf = 4 if self.two_shot else 2      # partials x2 (+ results x2)
+        total = self.flag_bytes + nbuf * self.buf_bytes
         # every rank must launch the same grid
         grids = [None] * world
         dist.all_gather_object(grids, self.grid, group=group)
@@ -78,9 +83,12 @@ class TPComm:
         self._flags = (ctypes.c_void_p * world)(*bases)
         self._bufs = [(ctypes.c_void_p * world)(*[b + self.flag_bytes + s * self.buf_bytes
                                                   for b in bases]) for s in (0, 1)]
+        self._results = [ctypes.cast((ctypes.c_void_p * world)(
+            *[b + self.flag_bytes + (2 + s) * self.buf_bytes for b in bases]), ctypes.c_void_p)
+            if self.two_shot else None for s in (0, 1)]
         self.buffers = [device_view(self._base + self.flag_bytes + s * self.buf_bytes,
                                     (max_rows, hidden), torch.bfloat16, device) for s in (0, 1)]
-        err_off = (world + 1) * self.grid * 4
+        err_off = (2 * world + 1) * self.grid * 4
         self._error = device_view(self._base + err_off, (1,), torch.int32, device)
         dist.barrier(group=group)
 
@@ -97,7 +105,7 @@ class TPComm:
         y = torch.empty((rows, H), dtype=torch.bfloat16, device=self.device)
         r_out = torch.empty_like(y)
         _native.call("vj_allreduce_add_rmsnorm", ctypes.cast(self._bufs[site], ctypes.c_void_p),
-                     ctypes.cast(self._flags, ctypes.c_void_p),
+                     self._results[site], ctypes.cast(self._flags, ctypes.c_void_p),
                      ctypes.c_void_p(self._base), self.rank, self.world, residual.data_ptr(),
                      weight.data_ptr(), r_out.data_ptr(), y.data_ptr(), rows, H, float(eps),
                      torch.cuda.current_stream(self.device).cuda_stream)
