@@ -86,7 +86,7 @@ def _check_comm(comm, rank, world, dev, H):
     comm.close()
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, engine_check=True):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, os.path.join(root, "vllm-jax_b200"))
@@ -102,7 +102,9 @@ def _worker(rank, world, port, q):
         for two_shot in (False, True):
             _check_comm(TPComm(dist.group.WORLD, rank, world, dev, R, H, two_shot=two_shot),
                         rank, world, dev, H)
-
+        if not engine_check:
+            q.put((rank, "ok"))
+            return
         # engine: NVLink path (CUDA-graph decode) vs NCCL path (eager)
         from vllm_b200 import Config, SamplingParams
         from vllm_b200.model.qwen3 import Qwen3Config, Qwen3Weights
@@ -136,17 +138,17 @@ def _worker(rank, world, port, q):
             dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_nvlink_fused_allreduce_two_ranks():
+def _run(world, engine_check):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, engine_check))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = {}
     try:
-        for _ in range(2):
+        for _ in range(world):
             rank, msg = q.get(timeout=420)
             results[rank] = msg
     finally:
@@ -154,4 +156,16 @@ def test_nvlink_fused_allreduce_two_ranks():
             p.join(timeout=60)
             if p.is_alive():
                 p.kill()
-    assert results == {0: "ok", 1: "ok"}, results
+    assert results == {r: "ok" for r in range(world)}, results
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_nvlink_fused_allreduce_two_ranks():
+    _run(2, True)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs 4 GPUs")
+def test_nvlink_fused_allreduce_all_ranks():
+    """Every GPU of the box (4 or 8 ranks), one-shot and two-shot."""
+    n = torch.cuda.device_count()
+    _run(8 if n >= 8 else 4, False)
