@@ -324,6 +324,7 @@ def run_ours(args, rank, world, local_rank):
         "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": round(total_ms / args.steps, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        # (the whole request set is fixed as N grows: strong scaling, also with dp > 1)
         "data": "synthetic (seeded C3 lengths/tables; K,V,q ~ N(0,1) bf16)",
         "config": {"workload": "C3 paged decode attention", "batch": B,
                    "num_q_heads": hq_all, "num_kv_heads": hkv_all, "head_dim": D,
@@ -627,14 +628,25 @@ def run_e2e(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     mcfg = get_config(cfg["model"])
-    prompts, outs = (c5_requests if c5 else c4_requests)(cfg, mcfg.vocab_size)
-    max_len = max(len(p) + o for p, o in zip(prompts, outs))
+    all_prompts, all_outs = (c5_requests if c5 else c4_requests)(cfg, mcfg.vocab_size)
+    max_len = max(len(p) + o for p, o in zip(all_prompts, all_outs))
+    # world = dp x tp: dp engine replicas, each tensor parallel over tp GPUs,
+    # request i served by replica i % dp
+    tp = args.tp or world
+    if world % tp:
+        raise SystemExit("--tp must divide the number of GPUs")
+    dp = world // tp
+    replica = rank // tp
+    pg = None
+    if world > 1:
+        groups = [dist.new_group(list(range(d * tp, (d + 1) * tp))) for d in range(dp)]
+        pg = groups[replica] if tp > 1 else None
+    prompts, outs = all_prompts[replica::dp], all_outs[replica::dp]
     econf = Config(model=cfg["model"], max_num_batched_tokens=cfg["max_num_batched_tokens"],
                    max_num_seqs=cfg["max_num_seqs"], num_blocks=0, block_size=16,
-                   tensor_parallel_size=world, gpu_memory_utilization=0.9,
+                   tensor_parallel_size=tp, gpu_memory_utilization=0.9,
                    max_model_len=((max_len + 15) // 16) * 16, compat=False,
                    enable_chunked_prefill=c5)
-    pg = dist.group.WORLD if world > 1 else None
 
     def progress(msg):
         print(f"[rank {rank}] {msg}", file=sys.stderr, flush=True)
@@ -672,13 +684,13 @@ def run_e2e(args, rank, world, local_rank):
     wall = float(t.item())
     if rank != 0:
         return
-    value = sum(outs) / wall
+    value = sum(all_outs) / wall
     st = stats[-1]
     peaks, src = load_peaks()
     # decode-step roofline: weights of one rank + K/V of every context token per step
     wbytes = sum(p.numel() * 2 for lw in eng.weights.layers for p in
                  (lw.w_qkv, lw.w_o, lw.w_gate_up, lw.w_down)) + eng.weights.lm_head.numel() * 2
-    kvb = mcfg.num_hidden_layers * 2 * (mcfg.num_key_value_heads // world) * mcfg.head_dim * 2
+    kvb = mcfg.num_hidden_layers * 2 * (mcfg.num_key_value_heads // tp) * mcfg.head_dim * 2
     dec_bytes = st["decode_steps"] * wbytes + st["decode_ctx_tokens"] * kvb
     achieved = dec_bytes / max(st["decode_s"], 1e-9) / 1e9
     if c5:
@@ -697,12 +709,13 @@ def run_e2e(args, rank, world, local_rank):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded random token ids and lengths; random-init N(0,0.02) weights)",
         "config": {"workload": workload, "model": cfg["model"],
-                   "num_requests": cfg["num_requests"], "output_tokens": sum(outs),
-                   "prompt_tokens": sum(len(p) for p in prompts),
+                   "num_requests": cfg["num_requests"], "output_tokens": sum(all_outs),
+                   "prompt_tokens": sum(len(p) for p in all_prompts),
                    "chunked_prefill": c5,
                    "max_num_batched_tokens": cfg["max_num_batched_tokens"],
                    "max_num_seqs": cfg["max_num_seqs"], "num_blocks": eng.config.num_blocks,
-                   "parallelism": f"tp{world}" if world > 1 else "single GPU",
+                   "parallelism": (f"dp{dp}x" if dp > 1 else "") + f"tp{tp}" if world > 1
+                   else "single GPU",
                    "engine_steps": st["steps"], "decode_steps": st["decode_steps"],
                    "prefill_s": round(st["prefill_s"], 3), "decode_s": round(st["decode_s"], 3),
                    "l2": "decode steps stream all weights + KV (> L2)"},
@@ -729,6 +742,9 @@ def main():
     ap.add_argument("--workload", choices=["decode", "prefill", "e2e", "c5"], default="decode")
     ap.add_argument("--model", default=None, help="e2e: model preset (default Qwen3-8B)")
     ap.add_argument("--max-num-seqs", type=int, default=None, help="e2e: scheduler seats")
+    ap.add_argument("--tp", type=int, default=None,
+                    help="e2e/c5: tensor-parallel degree (default all GPUs); the rest is "
+                         "data parallel (engine replicas, requests split round-robin)")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--ref-budget", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
