@@ -8,14 +8,15 @@ decode HBM GB/s (algorithmic bytes / time). One "step" = one decode-attention
 call over the whole batch (all KV heads of all sequences).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|prefill|e2e|c5]
+                    [--workload decode|prefill|kvstore|e2e|c5] [--tp T]
 
 N > 1 (torchrun, one process per GPU): tensor parallel by KV head -- rank r
 owns KV heads [r*8/N, (r+1)*8/N) of the same batch (its own pool slice); no
 collective on the data path. Total work is fixed, so scaling is "strong";
 `value` = algorithmic bytes of all ranks / max-over-ranks device time.
 
---workload prefill: C2 paged prefill attention (TFLOP/s). --workload e2e: C4,
+--workload prefill: C2 paged prefill attention (TFLOP/s). --workload kvstore:
+K3 (q/k norm + RoPE + KV scatter) on the C2 batch (GB/s). --workload e2e: C4,
 Qwen3-8B continuous batching through Engine.generate (output tok/s).
 --workload c5: C5, Qwen3-32B with chunked prefill mixed with decode (output
 tok/s; --batch R runs the first R of the 1024 requests, and says so).
@@ -324,7 +325,6 @@ def run_ours(args, rank, world, local_rank):
         "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": round(total_ms / args.steps, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        # (the whole request set is fixed as N grows: strong scaling, also with dp > 1)
         "data": "synthetic (seeded C3 lengths/tables; K,V,q ~ N(0,1) bf16)",
         "config": {"workload": "C3 paged decode attention", "batch": B,
                    "num_q_heads": hq_all, "num_kv_heads": hkv_all, "head_dim": D,
@@ -350,6 +350,163 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
     if pool is not None:
         pool.terminate()
+
+
+def _cpu_kvstore_chunk(args):
+    T, hq, hkv, seed = args
+    from oracle import kv_store as okv
+    from oracle.bf16 import bf16
+    rng = np.random.default_rng(seed)
+    d = 128
+    q = bf16(rng.standard_normal((T, hq, d)))
+    k = bf16(rng.standard_normal((T, hkv, d)))
+    v = bf16(rng.standard_normal((T, hkv, d)))
+    ones = np.ones(d, np.float32)
+    kc = np.zeros(((T + 15) // 16, 16, hkv, d), np.float32)
+    vc = np.zeros_like(kc)
+    pos = rng.integers(0, 6000, T).astype(np.int32)
+    t0 = time.perf_counter()
+    okv.kv_store_qknorm_rope(q, k, v, ones, ones, pos, np.arange(T, dtype=np.int32), kc, vc)
+    return time.perf_counter() - t0
+
+
+def kvstore_bytes(T: int, hq: int, hkv: int, d: int = 128) -> int:
+    """Algorithmic HBM bytes of one K3 call: q, k, v rows read; q_out and the
+    K/V slots written; positions and slots read (norm weights and the RoPE
+    frequencies are a few hundred bytes)."""
+    return T * ((hq + 2 * hkv) * d * 2 + (hq + 2 * hkv) * d * 2 + 8)
+
+
+def run_kvstore(args, rank, world, local_rank):
+    """K3 on the C2 prefill batch: q/k RMSNorm + RoPE + KV-slot scatter of all
+    new tokens of the 64 C2 sequences (positions prefix + i, slots from the C2
+    block tables), Qwen3-8B heads. HBM-bound: one read and one write of every
+    row. N > 1: TP by KV head (each rank its heads of every token)."""
+    import torch
+    import torch.distributed as dist
+    from vllm_b200.kernels.kv_store import kv_store_qknorm_rope
+
+    cfg = C2
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    hq_all, hkv_all, D, bs = cfg["num_q_heads"], cfg["num_kv_heads"], cfg["head_dim"], 16
+    if hkv_all % world:
+        raise SystemExit(f"--gpus {world} must divide {hkv_all} KV heads")
+    hq, hkv = hq_all // world, hkv_all // world
+    new, pre, bt = c2_batch()
+    pos_l, slot_l = [], []
+    for s_, (n, p) in enumerate(zip(new, pre)):
+        t = np.arange(p, p + n)
+        pos_l.append(t)
+        slot_l.append(bt[s_, t // bs] * bs + t % bs)
+    positions = np.concatenate(pos_l).astype(np.int32)
+    slots = np.concatenate(slot_l).astype(np.int32)
+    T = len(slots)
+    nb = cfg["pool_blocks"]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2000 + rank)
+    kv_cache = torch.zeros((2, nb, bs, hkv, D), dtype=torch.bfloat16, device=dev)
+    q = torch.randn((T, hq, D), generator=gen, device=dev).to(torch.bfloat16)
+    k = torch.randn((T, hkv, D), generator=gen, device=dev).to(torch.bfloat16)
+    v = torch.randn((T, hkv, D), generator=gen, device=dev).to(torch.bfloat16)
+    qw = torch.ones(D, dtype=torch.bfloat16, device=dev)
+    kw = torch.ones(D, dtype=torch.bfloat16, device=dev)
+    d_pos = torch.from_numpy(positions).to(dev)
+    d_slot = torch.from_numpy(slots).to(dev)
+    q_out = torch.empty_like(q)
+
+    def step():
+        kv_store_qknorm_rope(q, k, v, kv_cache, d_slot, d_pos, qw, kw, q_out=q_out)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    stream = torch.cuda.current_stream(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        t_start.record(stream)
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            step()
+            ev[i][1].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    total_ms = t_start.elapsed_time(t_end)
+    per_launch_ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
+    # e2e: the projected rows come from pinned host memory, q_out goes back
+    h_q, h_k, h_v = q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()
+    h_pos, h_slot = d_pos.cpu().pin_memory(), d_slot.cpu().pin_memory()
+    h_out = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    e_q, e_k, e_v = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    e_pos, e_slot = torch.empty_like(d_pos), torch.empty_like(d_slot)
+
+    def e2e_step():
+        for dst, src in ((e_q, h_q), (e_k, h_k), (e_v, h_v), (e_pos, h_pos), (e_slot, h_slot)):
+            dst.copy_(src, non_blocking=True)
+        kv_store_qknorm_rope(e_q, e_k, e_v, kv_cache, e_slot, e_pos, qw, kw, q_out=q_out)
+        h_out.copy_(q_out, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    t = torch.tensor([total_ms, per_launch_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, per_launch_ms, e2e_ms = t.tolist()
+    if rank != 0:
+        return
+    step_bytes = kvstore_bytes(T, hq_all, hkv_all)
+    rank_bytes = kvstore_bytes(T, hq, hkv)
+    peaks, peak_src = load_peaks()
+    achieved = rank_bytes / (per_launch_ms / 1e3) / 1e9
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        import multiprocessing as mproc
+        cores = max(1, min(16, len(os.sched_getaffinity(0))))
+        chunk, n_chunks = 4096, 8 * cores          # ~0.5 s per chunk: a few seconds per core
+        with mproc.get_context("spawn").Pool(cores) as pool:
+            pool.map(_cpu_kvstore_chunk, [(256, hq_all, hkv_all, i) for i in range(cores)])
+            t0 = time.perf_counter()
+            pool.map(_cpu_kvstore_chunk, [(chunk, hq_all, hkv_all, i) for i in range(n_chunks)])
+            wall = time.perf_counter() - t0
+        cpu = {"value": round(kvstore_bytes(chunk * n_chunks, hq_all, hkv_all) / wall / 1e9, 3),
+               "unit": "GB/s", "cores": cores, "kind": "port",
+               "sample": f"{n_chunks} chunks of {chunk} tokens over {cores} processes "
+                         "(oracle.kv_store)"}
+    h2d = (h_q.numel() + h_k.numel() + h_v.numel()) * 2 + (h_pos.numel() + h_slot.numel()) * 4
+    line = {
+        "metric": "KV-scatter + q/k RMSNorm + RoPE HBM GB/s (K3 on the C2 batch, Qwen3-8B heads)",
+        "value": round(step_bytes * args.steps / (total_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (C2 positions/slots; q,k,v ~ N(0,1) bf16)",
+        "config": {"workload": "K3 kv_store_qknorm_rope on the C2 batch", "tokens": T,
+                   "num_q_heads": hq_all, "num_kv_heads": hkv_all, "head_dim": D,
+                   "parallelism": f"tp{world} by KV head" if world > 1 else "single GPU",
+                   "l2": f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB per step)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "peak_source": f"{peak_src} hbm_gbs", "kernel": "kv_store_qknorm_rope_kernel",
+                     "traffic": None},
+        "e2e": {"value": round(step_bytes * args.steps / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h_out.numel() * 2},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
 
 
 def _cpu_prefill_seq(args):
@@ -739,7 +896,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "prefill", "e2e", "c5"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "prefill", "kvstore", "e2e", "c5"],
+                    default="decode")
     ap.add_argument("--model", default=None, help="e2e: model preset (default Qwen3-8B)")
     ap.add_argument("--max-num-seqs", type=int, default=None, help="e2e: scheduler seats")
     ap.add_argument("--tp", type=int, default=None,
@@ -774,6 +932,8 @@ def main():
     try:
         if args.workload == "prefill":
             run_prefill(args, rank, world, local_rank)
+        elif args.workload == "kvstore":
+            run_kvstore(args, rank, world, local_rank)
         elif args.workload in ("e2e", "c5"):
             if args.steps > 3:
                 args.steps = 1      # one generate() of the whole request set per step

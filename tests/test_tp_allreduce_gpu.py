@@ -76,3 +76,40 @@ def test_fused_allreduce_rejects_bad_arguments():
                                       ctypes.cast(null, ctypes.c_void_p), None, 0, 2, None,
                                       None, None, None, 4, 10000, 1e-6, None)
     assert st == _native.VJ_ERR_UNSUPPORTED
+
+
+def test_peer_wait_times_out_into_the_error_word():
+    """A peer that never announces: every CTA's wait gives up after its bound
+    (2 s), sets the error word and returns; the context stays usable. One
+    launch on one GPU with a flag nothing sets -- no second kernel waits on it."""
+    import time
+
+    from vllm_b200 import _native
+    from vllm_b200.kernels.fused import add_rmsnorm
+    from vllm_b200.src.tp_comm import device_view
+    lib = _native.load()
+    dev = torch.device("cuda", 0)
+    G = int(lib.vj_tp_grid())
+    world, rows, hidden = 2, 4, 1024
+    regions = [_region(lib, world, rows, hidden) for _ in range(world)]
+    bufs = (ctypes.c_void_p * world)(*[b + fb for b, fb, _ in regions])
+    flags = (ctypes.c_void_p * world)(*[b for b, _, _ in regions])
+    x = torch.ones(rows, hidden, dtype=torch.bfloat16, device=dev)
+    w = torch.ones(hidden, dtype=torch.bfloat16, device=dev)
+    xo, y = torch.empty_like(x), torch.empty_like(x)
+    t0 = time.perf_counter()
+    _native.call("vj_allreduce_add_rmsnorm", ctypes.cast(bufs, ctypes.c_void_p), None,
+                 ctypes.cast(flags, ctypes.c_void_p), ctypes.c_void_p(regions[0][0]), 0, world,
+                 x.data_ptr(), w.data_ptr(), xo.data_ptr(), y.data_ptr(), rows, hidden, 1e-6,
+                 torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    err = device_view(regions[0][0] + (2 * world + 1) * G * 4, (1,), torch.int32, dev)
+    assert int(err.item()) == 1
+    assert 1.5 < waited < 30
+    # the device still works
+    r, h = add_rmsnorm(x, w, 1e-6, residual=x)
+    torch.cuda.synchronize()
+    assert torch.isfinite(h.float()).all()
+    for base, _, _ in regions:
+        _native.check(lib.vj_comm_free(ctypes.c_void_p(base)))
