@@ -907,14 +907,16 @@ def main():
     ap.add_argument("--ref-budget", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
-                    help="profiling only: first B sequences of the C3 batch")
+                    help="profiling only: B sequences of the C3 / C2 batch (e2e: requests)")
     ap.add_argument("--pool-blocks", type=int, default=None,
-                    help="profiling only: KV pool size in blocks")
+                    help="profiling only: KV pool size in blocks (C3 / C2)")
     args = ap.parse_args()
     if args.batch is not None:
         C3["batch"] = args.batch
+        C2["num_seqs"] = args.batch
     if args.pool_blocks is not None:
         C3["pool_blocks"] = args.pool_blocks
+        C2["pool_blocks"] = args.pool_blocks
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

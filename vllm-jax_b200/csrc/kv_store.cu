@@ -28,6 +28,13 @@ constexpr int kHeadDim = 128;
 constexpr int kPairs = kHeadDim / 2;
 constexpr int kRowsPerHw = 6;   // rows in flight per half-warp (96 heads per pass)
 
+// Elementwise product of two bf16x2 words, each lane rounded to nearest even.
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 struct RopeTable {
   float inv_freq[kPairs];  // bf16-valued
 };
@@ -66,7 +73,8 @@ kv_store_qknorm_rope_kernel(const __nv_bfloat16 *__restrict__ q_in,
                             int block_size, int64_t sb, int64_t st, int64_t sh,
                             int64_t qrs, int64_t krs, int64_t vrs,
                             float eps, int flags, RopeTable rope) {
-  __shared__ float2 cs[kPairs];
+  // per pair: bf16x2 words (cos, sin) and (sin, cos)
+  __shared__ uint2 cs[kPairs];
   const int64_t t = blockIdx.x;
   const int tid = threadIdx.x;
   const bool do_norm = (flags & VJ_KV_NORM) != 0;
@@ -100,7 +108,8 @@ kv_store_qknorm_rope_kernel(const __nv_bfloat16 *__restrict__ q_in,
         const float f = round_bf16(pos * rope.inv_freq[tid]);
         double s, c;
         sincos(static_cast<double>(f), &s, &c);
-        cs[tid] = make_float2(bf16_from_f64(c), bf16_from_f64(s));
+        const float cb = bf16_from_f64(c), sb = bf16_from_f64(s);
+        cs[tid] = make_uint2(pack_bf16(cb, sb), pack_bf16(sb, cb));  // exact: bf16 values
       }
       __syncthreads();
     }
@@ -114,20 +123,21 @@ kv_store_qknorm_rope_kernel(const __nv_bfloat16 *__restrict__ q_in,
       uint32_t wd[4] = {raw[k].x, raw[k].y, raw[k].z, raw[k].w};
       if (kind != 2) {
         const __nv_bfloat16 *w = kind == 0 ? q_w : k_w;
-        float x[8];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) { x[2 * j] = bf16_lo(wd[j]); x[2 * j + 1] = bf16_hi(wd[j]); }
         if (do_norm) {
           // flax RMSNorm: y = bf16(x * (rsqrt(mean(x^2) + eps) * scale)), fp32
           double ss = 0.0;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) ss += static_cast<double>(x[j]) * x[j];
+          for (int j = 0; j < 4; ++j) {
+            const double lo = bf16_lo(wd[j]), hi = bf16_hi(wd[j]);
+            ss += lo * lo + hi * hi;
+          }
           // the two half-warps of a warp may hold different kinds of rows
           // (odd head counts under tensor parallelism): reduce within the half
           const unsigned half_mask = 0xffffu << (16 * (hw & 1));
 #pragma unroll
           for (int o = 8; o >= 1; o >>= 1) ss += __shfl_xor_sync(half_mask, ss, o);
-          const float ms = __fdiv_rn(static_cast<float>(ss), static_cast<float>(kHeadDim));
+          // mean = sum / 128: a power-of-two scale, exact as a multiply
+          const float ms = __fmul_rn(static_cast<float>(ss), 1.0f / kHeadDim);
           const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
           const uint4 wr = __ldg(reinterpret_cast<const uint4 *>(w + l16 * 8));
           const uint32_t ww[4] = {wr.x, wr.y, wr.z, wr.w};
@@ -135,26 +145,23 @@ kv_store_qknorm_rope_kernel(const __nv_bfloat16 *__restrict__ q_in,
           for (int j = 0; j < 4; ++j) {
             const float m0 = __fmul_rn(inv, bf16_lo(ww[j]));
             const float m1 = __fmul_rn(inv, bf16_hi(ww[j]));
-            x[2 * j] = round_bf16(__fmul_rn(x[2 * j], m0));
-            x[2 * j + 1] = round_bf16(__fmul_rn(x[2 * j + 1], m1));
+            wd[j] = pack_bf16(__fmul_rn(bf16_lo(wd[j]), m0), __fmul_rn(bf16_hi(wd[j]), m1));
           }
         }
         if (do_rope) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const float2 c = cs[l16 * 4 + j];  // (cos, sin)
-            const float x1 = x[2 * j], x2 = x[2 * j + 1];
-            // stack((x1*cos - x2*sin, x1*sin + x2*cos), -1): every op rounds to bf16
-            const float a = round_bf16(__fmul_rn(x1, c.x));
-            const float b = round_bf16(__fmul_rn(x2, c.y));
-            const float d = round_bf16(__fmul_rn(x1, c.y));
-            const float e = round_bf16(__fmul_rn(x2, c.x));
-            x[2 * j] = round_bf16(__fsub_rn(a, b));
-            x[2 * j + 1] = round_bf16(__fadd_rn(d, e));
+            // pair (x1, x2) = word j; stack((x1*cos - x2*sin, x1*sin + x2*cos), -1)
+            // with every op rounded to bf16: the products of bf16 values are
+            // exact before their rounding, so bf16x2 multiplies give the same
+            // bits; the sum and difference round through fp32 as before
+            const uint2 c = cs[l16 * 4 + j];
+            const uint32_t ab = bf16x2_mul(wd[j], c.x);   // (x1*cos, x2*sin)
+            const uint32_t de = bf16x2_mul(wd[j], c.y);   // (x1*sin, x2*cos)
+            wd[j] = pack_bf16(__fsub_rn(bf16_lo(ab), bf16_hi(ab)),
+                              __fadd_rn(bf16_lo(de), bf16_hi(de)));
           }
         }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) wd[j] = pack_bf16(x[2 * j], x[2 * j + 1]);
       }
       const uint4 outv = make_uint4(wd[0], wd[1], wd[2], wd[3]);
       if (kind == 0) {
