@@ -211,10 +211,20 @@ def cpu_decode_baseline(lens: np.ndarray, hkv: int, hq: int, budget_s: float, po
                       f"{t_cpu:.1f} s of compute over {cores} processes"}
 
 
-def make_pool():
+def _one_blas_thread():
+    """Pool initializer: one BLAS thread per worker process, so that N
+    processes use N cores instead of oversubscribing them N x N."""
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(1)
+    except ImportError:
+        pass
+
+
+def make_pool(n: int | None = None):
     import multiprocessing as mp
-    n = len(os.sched_getaffinity(0))
-    return mp.get_context("spawn").Pool(n)
+    n = n or len(os.sched_getaffinity(0))
+    return mp.get_context("spawn").Pool(n, initializer=_one_blas_thread)
 
 
 # ---------------------------------------------------------------------------
@@ -471,10 +481,9 @@ def run_kvstore(args, rank, world, local_rank):
     achieved = rank_bytes / (per_launch_ms / 1e3) / 1e9
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        import multiprocessing as mproc
         cores = max(1, min(16, len(os.sched_getaffinity(0))))
         chunk, n_chunks = 4096, 8 * cores          # ~0.5 s per chunk: a few seconds per core
-        with mproc.get_context("spawn").Pool(cores) as pool:
+        with make_pool(cores) as pool:
             pool.map(_cpu_kvstore_chunk, [(256, hq_all, hkv_all, i) for i in range(cores)])
             t0 = time.perf_counter()
             pool.map(_cpu_kvstore_chunk, [(chunk, hq_all, hkv_all, i) for i in range(n_chunks)])
