@@ -203,3 +203,27 @@ def test_engine_loads_a_local_hf_checkpoint(tmp_path):
                weights=Qwen3Weights(cfg, dev, seed=4, gen_device="cpu"),
                max_slots=4).generate(prompts, sp)
     assert a == b
+
+
+def test_lookahead_scheduling_matches_synchronous_steps():
+    """generate() with async_scheduling (step k+1 enqueued before step k's
+    tokens are read) gives the same tokens as the synchronous loop."""
+    from vllm_b200 import Config, SamplingParams
+    from vllm_b200.model.qwen3 import Qwen3Config, Qwen3Weights
+    from vllm_b200.src.engine import Engine
+    cfg = Qwen3Config(hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                      num_attention_heads=16, vocab_size=1000, tie_word_embeddings=True)
+    dev = torch.device("cuda", 0)
+    w = Qwen3Weights(cfg, dev, seed=6)
+    rng = np.random.default_rng(5)
+    prompts = [rng.integers(0, 1000, n).tolist() for n in (46, 17, 20, 28, 19, 58, 5)]
+    outs = []
+    for async_on in (False, True):
+        eng = Engine(Config(model="tiny", max_num_batched_tokens=256, max_num_seqs=4,
+                            num_blocks=40, block_size=16, compat=False,
+                            async_scheduling=async_on), dev, model_config=cfg, weights=w,
+                     max_slots=16)
+        assert eng.async_scheduling == async_on
+        outs.append(eng.generate(prompts, SamplingParams(temperature=0, max_new_tokens=21,
+                                                         ignore_eos=True)))
+    assert outs[0] == outs[1]

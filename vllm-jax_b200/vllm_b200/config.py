@@ -30,6 +30,10 @@ class Config:
     # fused peer-memory kernel (CUDA-graph capturable), "nccl" always uses
     # torch.distributed all-reduce (decode then runs eagerly).
     tp_allreduce: str = "nvlink"
+    # With compat=False (and without chunked prefill) generate() schedules
+    # step k+1 before reading step k's tokens back, so host work overlaps the
+    # GPU; a request that samples EOS is computed one extra, discarded step.
+    async_scheduling: bool = True
 
     @property
     def max_len(self) -> int:

@@ -77,18 +77,35 @@ class DeviceTables:
         self.num_blocks = torch.zeros(max_slots, dtype=torch.int32, device=device)
         self.error = torch.zeros(1, dtype=torch.int32, device=device)
         self._last_extra = None
-        self._pinned = torch.empty(1 << 16, dtype=torch.int32).pin_memory()
+        # pinned upload buffers in a ring: a buffer is rewritten only after the
+        # copy that last read it has completed (its event), so the host never
+        # waits for the GPU to drain before preparing the next step
+        self._ring = [torch.empty(1 << 14, dtype=torch.int32).pin_memory() for _ in range(8)]
+        self._ring_events: list[torch.cuda.Event | None] = [None] * len(self._ring)
+        self._ring_next = 0
         self._staging = torch.empty(1 << 16, dtype=torch.int32, device=device)
 
     def _upload(self, arr: np.ndarray) -> torch.Tensor:
+        """Copy int32 words to the device staging buffer (stream-ordered: the
+        copy lands after every kernel enqueued before it, so views returned by
+        an earlier upload stay valid for the kernels enqueued in between)."""
         n = arr.size
-        if n > self._pinned.numel():
-            self._pinned = torch.empty(2 * n, dtype=torch.int32).pin_memory()
+        i = self._ring_next
+        self._ring_next = (i + 1) % len(self._ring)
+        ev = self._ring_events[i]
+        if ev is not None:
+            ev.synchronize()
+        if n > self._ring[i].numel():
+            self._ring[i] = torch.empty(2 * n, dtype=torch.int32).pin_memory()
+        if n > self._staging.numel():
             self._staging = torch.empty(2 * n, dtype=torch.int32, device=self.device)
-        # the previous step's copy out of the pinned buffer must be done first
-        torch.cuda.current_stream(self.device).synchronize()
-        self._pinned[:n].numpy()[:] = arr
-        self._staging[:n].copy_(self._pinned[:n], non_blocking=True)
+        buf = self._ring[i]
+        buf[:n].numpy()[:] = arr
+        stream = torch.cuda.current_stream(self.device)
+        self._staging[:n].copy_(buf[:n], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        self._ring_events[i] = ev
         return self._staging[:n]
 
     def _scatter(self, rows: list[tuple[int, int, list[int]]], table: torch.Tensor,

@@ -178,6 +178,90 @@ class Engine:
                 del self.live[r.id]
         return done
 
+    # ---------------------------------------------------------------- async loop
+    @property
+    def async_scheduling(self) -> bool:
+        c = self.config
+        return c.async_scheduling and not c.compat and not c.enable_chunked_prefill
+
+    def _finish(self, r: Request) -> None:
+        """Scheduler.postprocess's finish (compat=False: blocks released)."""
+        from .request import Status
+        r.status = Status.FINISHED
+        sched = self.scheduler
+        if r in sched.running:
+            sched.running.remove(r)
+        elif r in sched.waiting:              # preempted before its EOS was read
+            sched.waiting.remove(r)
+        sched.finished_requests.append(r)
+        self.kv.deallocate(r)
+        self.runner.release(r)
+        self.live.pop(r.id, None)
+
+    def _launch(self):
+        """Schedule and enqueue one step while the previous one still runs.
+        Decode rows get a placeholder token at once (the real one is already
+        on its way into the device token table, which the next step reads);
+        a request that reaches max_new_tokens finishes now."""
+        decode, prefill = self.scheduler.schedule()
+        if not decode and not prefill:
+            return None
+        st = self.stats
+        t0 = time.perf_counter()
+        st["decode_ctx_tokens"] += sum(len(r) for r in decode)
+        pending = self.runner.launch(decode, prefill, self.live, st)
+        slots = []
+        for r in decode:
+            r.token_ids.append(-1)
+            r.num_completion_tokens += 1
+            slots.append(len(r.token_ids) - 1)
+            if r.num_completion_tokens == r.max_new_tokens:
+                self._finish(r)
+        st["steps"] += 1
+        st["decode_tokens"] += len(decode)
+        st["decode_steps"] += 1 if decode else 0
+        st["prefill_tokens"] += sum(len(r) for r in prefill)
+        return decode, slots, pending, bool(prefill), t0
+
+    def _complete(self, step) -> None:
+        """Fill a step's placeholders; a request that sampled EOS finishes
+        here, and the token a later step already computed for it is dropped."""
+        decode, slots, pending, had_prefill, t0 = step
+        if pending is not None:
+            for r, i, t in zip(decode, slots, pending.collect()):
+                if i >= len(r.token_ids):          # stopped at an earlier EOS
+                    continue
+                r.token_ids[i] = t
+                if not r.ignore_eos and t == r.eos_token_id:
+                    del r.token_ids[i + 1:]
+                    r.num_completion_tokens = len(r.token_ids) - r.num_prompt_tokens
+                    if not r.is_finished():
+                        self._finish(r)
+        # wall time partitioned between steps (launches overlap earlier steps)
+        now = time.perf_counter()
+        key = "prefill_s" if had_prefill else "decode_s"
+        self.stats[key] += now - max(t0, self._last_done)
+        self._last_done = now
+
+    def _run_async(self) -> None:
+        """generate()'s loop with one step of lookahead: step k+1 is scheduled
+        and enqueued before step k's tokens are read back, so host scheduling
+        overlaps the GPU. Only EOS needs step k's tokens; a request that hits
+        it is computed one extra step whose token is discarded."""
+        pending = None
+        self._last_done = time.perf_counter()
+        while True:
+            nxt = None if self.scheduler.is_finished() else self._launch()
+            if pending is not None:
+                self._complete(pending)
+            elif nxt is None:
+                if self.scheduler.is_finished():
+                    break
+                raise RuntimeError("scheduler made no progress (pool too small?)")
+            pending = nxt
+            if pending is None and self.scheduler.is_finished():
+                break
+
     def generate(self, prompts, sampling_params: SamplingParams | list | None = None,
                  **kwargs):
         """vllm/src/engine.py:45-75. Returns, per prompt, the completion text
@@ -195,8 +279,11 @@ class Engine:
             r.sample_stream = i
             reqs.append(r)
             self.add_request(r)
-        while not self.scheduler.is_finished():
-            self.step()
+        if self.async_scheduling:
+            self._run_async()
+        else:
+            while not self.scheduler.is_finished():
+                self.step()
         if self.tp_comm is not None and self.tp_comm.failed():
             raise RuntimeError("tensor-parallel all-reduce timed out waiting for a peer rank")
         outs = []

@@ -32,6 +32,17 @@ def kv_cache_bytes_per_block(mcfg: Qwen3Config, block_size: int, tp_size: int) -
             * mcfg.head_dim * 2)
 
 
+class PendingTokens:
+    """Sampled tokens of a launched step, copied to pinned host memory."""
+
+    def __init__(self, host: torch.Tensor, event: torch.cuda.Event, n: int):
+        self.host, self.event, self.n = host, event, n
+
+    def collect(self) -> list[int]:
+        self.event.synchronize()
+        return self.host[:self.n].tolist()
+
+
 def sampling_words(requests: list[Request]) -> np.ndarray | None:
     """Per-row sampling parameters as 32-bit words for one upload:
     temperature f32 [n], top_k i32 [n], top_p f32 [n], seeds u32 [n, 2].
@@ -87,7 +98,10 @@ class ModelRunner:
             tp_size == 1 or (tp_comm is not None and tp_comm.max_rows >= max_bucket))
         self.graphs: dict[int, tuple[torch.cuda.CUDAGraph, DecodeMeta, torch.Tensor]] = {}
         self.graph_launches: dict[int, int] = {}
-        self._tok_host = torch.empty(max(config.max_num_seqs, 1), dtype=torch.int32).pin_memory()
+        n = max(config.max_num_seqs, 1)
+        self._tok_ring = [torch.empty(n, dtype=torch.int32).pin_memory() for _ in range(4)]
+        self._tok_events: list[torch.cuda.Event | None] = [None] * 4
+        self._tok_next = 0
 
     # ------------------------------------------------------------------ state sync
     def _assign_slot(self, request: Request) -> int:
@@ -160,7 +174,27 @@ class ModelRunner:
                       words[2 * n:3 * n].view(torch.float32), words[3 * n:5 * n],
                       positions=d_lens, token_table=self.tables.tokens, slots=d_slots)
 
+    def _tokens_to_host(self, d_toks: torch.Tensor) -> "PendingTokens":
+        """Start the device->host copy of a step's tokens into a ring buffer."""
+        B = d_toks.numel()
+        i = self._tok_next
+        self._tok_next = (i + 1) % len(self._tok_ring)
+        if self._tok_events[i] is not None:
+            self._tok_events[i].synchronize()
+        if B > self._tok_ring[i].numel():
+            self._tok_ring[i] = torch.empty(B, dtype=torch.int32).pin_memory()
+        host = self._tok_ring[i]
+        host[:B].copy_(d_toks, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        self._tok_events[i] = ev
+        return PendingTokens(host, ev, B)
+
     def decode(self, requests: list[Request]) -> list[int]:
+        return self.decode_launch(requests).collect()
+
+    def decode_launch(self, requests: list[Request]) -> "PendingTokens":
+        """Enqueue one decode step; its tokens arrive through the returned handle."""
         slots = [r.slot for r in requests]
         lens = [len(r) for r in requests]
         B = len(requests)
@@ -178,11 +212,7 @@ class ModelRunner:
             logits = self.model.forward_decode(meta, self.kv_caches)
         d_slots, d_lens = self.tables.last_lists()
         toks = self._draw(logits[:B], d_slots, d_lens, self.tables.last_extra())
-        host = self._tok_host if B <= self._tok_host.numel() else torch.empty(
-            B, dtype=torch.int32).pin_memory()
-        host[:B].copy_(toks, non_blocking=True)
-        torch.cuda.current_stream(self.device).synchronize()
-        return host[:B].tolist()
+        return self._tokens_to_host(toks)
 
     # ------------------------------------------------------------------ prefill
     def prefill(self, requests: list[Request]) -> None:
@@ -191,6 +221,26 @@ class ModelRunner:
         self.model.forward_prefill(meta, self.kv_caches)
 
     # ------------------------------------------------------------------ step
+    def launch(self, decode_requests: list[Request], prefill_requests: list[Request],
+               live: dict[int, Request], stats: dict | None = None) -> "PendingTokens | None":
+        """Enqueue one engine step without waiting for it: the decode batch
+        (its tokens come back through the returned handle, not appended to the
+        requests), then the prefill batch. The host can schedule the next step
+        while this one runs; every later launch is ordered after it on the
+        stream."""
+        for r in prefill_requests:
+            if r.slot < 0 and stats is not None:
+                stats["h2d_bytes"] += 4 * len(r.token_ids)
+            self._assign_slot(r)
+        self._sync_blocks(live)
+        pending = self.decode_launch(decode_requests) if decode_requests else None
+        if prefill_requests:
+            self.prefill(prefill_requests)
+        if stats is not None:
+            stats["h2d_bytes"] += 8 * (len(decode_requests) + len(prefill_requests))
+            stats["d2h_bytes"] += 4 * len(decode_requests)
+        return pending
+
     def run(self, decode_requests: list[Request], prefill_requests: list[Request],
             live: dict[int, Request], stats: dict | None = None) -> list[int]:
         """One engine step (model_runner.py:310-333): decode batch first (its
@@ -261,11 +311,7 @@ class ModelRunner:
             if K:
                 d = self._draw(logits, meta.sample_slots, meta.sample_lens,
                                self.tables.last_extra())
-                host = self._tok_host if K <= self._tok_host.numel() else torch.empty(
-                    K, dtype=torch.int32).pin_memory()
-                host[:K].copy_(d, non_blocking=True)
-                torch.cuda.current_stream(self.device).synchronize()
-                toks = host[:K].tolist()
+                toks = self._tokens_to_host(d).collect()
             sampled = [rows[i][0] for i in pick]
             if stats is not None:
                 torch.cuda.current_stream(self.device).synchronize()
