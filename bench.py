@@ -507,7 +507,10 @@ def run_kvstore(args, rank, world, local_rank):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                      "peak_source": f"{peak_src} hbm_gbs", "kernel": "kv_store_qknorm_rope_kernel",
-                     "traffic": None},
+                     "traffic": (int(KVSTORE_PROFILE["dram_bytes"] * T / KVSTORE_PROFILE["tokens"])
+                                 if world == 1 else None),
+                     "traffic_source": "ncu dram bytes of a 16-sequence C2 capture, scaled by "
+                                       "tokens"},
         "e2e": {"value": round(step_bytes * args.steps / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h_out.numel() * 2},
         "gpu_launches": args.steps,
@@ -691,7 +694,9 @@ def run_prefill(args, rank, world, local_rank):
 # context tokens; profiles/decode_chunk_kernel_c3.md): dram read + write bytes.
 # DRAM traffic grows with the context tokens streamed, so a full C3 launch is
 # scaled by its context-token count.
-DECODE_PROFILE = {"ctx_tokens": 402_759, "dram_bytes": 1_651_773_000 + 38_666_240}
+DECODE_PROFILE = {"ctx_tokens": 402_759, "dram_bytes": 1_651_833_000 + 23_638_016}
+# K3 (kv_store_qknorm_rope_kernel) on the first 16 C2 sequences, 34,069 tokens
+KVSTORE_PROFILE = {"tokens": 34_069, "dram_bytes": 419_022_592 + 374_849_536}
 
 
 def decode_traffic(ctx_tokens: int) -> int:
