@@ -125,9 +125,7 @@ def _worker(rank, world, port, q, engine_check=True):
             assert eng.runner.use_cuda_graphs == (mode == "nvlink")
             res[mode] = eng.generate(prompts, SamplingParams(temperature=0, max_new_tokens=8,
                                                              ignore_eos=True))
-            if eng.tp_comm is not None:
-                eng.runner.graphs.clear()
-                eng.tp_comm.close()
+            eng.close()
         assert [o[:2] for o in res["nvlink"]] == [o[:2] for o in res["nccl"]], res
         q.put((rank, "ok"))
     except Exception as e:  # report to the parent, never hang it

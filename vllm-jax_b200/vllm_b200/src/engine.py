@@ -116,6 +116,16 @@ class Engine:
                       "decode_s": 0.0, "prefill_s": 0.0, "decode_ctx_tokens": 0,
                       "h2d_bytes": 0, "d2h_bytes": 0}
 
+    def close(self) -> None:
+        """Release the decode CUDA graphs and, under tensor parallelism, the
+        NVLink communicator (collective: every rank calls it). Call before
+        torch.distributed.destroy_process_group."""
+        self.runner.graphs.clear()
+        if self.tp_comm is not None:
+            self.tp_comm.close()
+            self.tp_comm = None
+            self.runner.model.tp_comm = None
+
     # ---------------------------------------------------------------- requests
     def preprocess(self, prompt) -> list[int]:
         if isinstance(prompt, str):
