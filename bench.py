@@ -853,6 +853,7 @@ def run_e2e(args, rank, world, local_rank):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     wall = float(t.item())
+    eng.close()       # every rank: graphs and the NVLink communicator
     if rank != 0:
         return
     value = sum(all_outs) / wall
