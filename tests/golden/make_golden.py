@@ -1,6 +1,7 @@
 """Generate host-side golden traces by running the reference's OWN Python code.
 
-Imports, from a vllm-jax checkout (default /root/reference, or $VLLM_JAX_REF):
+Imports, from the vllm-jax checkout named by $VLLM_JAX_REF (or the first
+command-line argument):
   vllm/src/request.py, vllm/src/kv_cache_manager.py, vllm/src/scheduler.py,
   vllm/config.py, vllm/sampling_params.py      -- unmodified, pure Python
   vllm/src/model_runner.py                      -- its prepare_prefill /
@@ -16,7 +17,7 @@ The reference cannot be imported under its own package name here (an
 unrelated `vllm` distribution is installed), so its modules are loaded from
 their files into a private `vllm` namespace inside this process only.
 
-Run:  python tests/golden/make_golden.py
+Run:  VLLM_JAX_REF=<vllm-jax checkout> python tests/golden/make_golden.py
 """
 from __future__ import annotations
 
@@ -31,7 +32,7 @@ from pathlib import Path
 
 import numpy as np
 
-REF = Path(os.environ.get("VLLM_JAX_REF", "/root/reference"))
+REF = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("VLLM_JAX_REF", "."))
 OUT = Path(__file__).resolve().parent / "host_traces.json"
 
 
