@@ -125,6 +125,22 @@ VJ_API vj_status vj_paged_decode(
     float scale, int32_t max_chunks, void *workspace, size_t workspace_bytes,
     cudaStream_t stream);
 
+/* vj_paged_decode without its planning launch: the workspace must hold the
+ * plan of an earlier vj_paged_decode call on the same stream with the same
+ * batch, context_lens values, num_kv_heads, bt_width, block_size and
+ * max_chunks, with no call that used this workspace for another batch in
+ * between. A decode step calls vj_paged_decode for its first layer and this
+ * for the other layers (their lengths are the same). No counterpart in the
+ * reference. */
+VJ_API vj_status vj_paged_decode_planned(
+    const void *q, const void *k_cache, const void *v_cache,
+    const int32_t *block_tables, const int32_t *context_lens, void *out,
+    int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+    int64_t num_blocks, int32_t block_size, int32_t bt_width, int32_t bt_stride,
+    int64_t stride_block, int64_t stride_token, int64_t stride_head,
+    float scale, int32_t max_chunks, void *workspace, size_t workspace_bytes,
+    cudaStream_t stream);
+
 /* ---------------------------------------------------------------------------
  * K2 for callers that cannot allocate device memory. No counterpart in the
  * reference: it exists for callers such as a custom-call handler inside an

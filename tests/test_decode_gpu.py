@@ -131,3 +131,24 @@ def test_paged_decode_large_batch_properties():
     _check(o1[:8].float().cpu().numpy(), ref)
     vmax = float(np.abs(cache[1]).max())
     assert float(o1.float().abs().max()) <= vmax + 1e-2
+
+
+def test_planned_decode_reuses_the_plan_of_the_first_call():
+    """vj_paged_decode_planned (the layers after the first of a decode step)
+    skips the planning launch and gives the oracle's result for new q, K and
+    V with the same lengths, several times in a row."""
+    from vllm_b200.kernels.decode_paged_attention import decode_workspace_bytes, paged_decode
+    B, Hq, Hkv, bs = 6, 32, 8, 16
+    lens = [0, 700, 33, 5000, 16, 2049]
+    nb = sum((L + bs - 1) // bs for L in lens) + 7
+    width = max((L + bs - 1) // bs for L in lens) + 3
+    ws = torch.empty(decode_workspace_bytes(B, Hq), dtype=torch.uint8, device="cuda")
+    scale = 1.0 / math.sqrt(128)
+    for layer in range(4):
+        q, cache, bt, ln = _make(B, Hq, Hkv, lens, nb, bs, width, seed=77 + layer)
+        ref = oatt.decode_attention(q, cache[0], cache[1], bt, ln, scale)
+        out = torch.full(q.shape, float("nan"), dtype=torch.bfloat16, device="cuda")
+        out = paged_decode(_t(q), _t(cache), _t(bt, torch.int32), _t(ln, torch.int32), scale,
+                           out=out, workspace=ws, reuse_plan=layer > 0)
+        torch.cuda.synchronize()
+        _check(out.float().cpu().numpy(), ref)

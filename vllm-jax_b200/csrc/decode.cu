@@ -371,6 +371,9 @@ __global__ void __launch_bounds__(256)
 decode_combine_kernel(DecodeArgs a) {
   const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
+  // the chunk kernel is done: rewind its work counter, so that a later call
+  // on the same stream may reuse this plan (vj_paged_decode_planned)
+  if (blockIdx.x == 0 && threadIdx.x == 0) a.ws.meta[2] = 0;
   if (wid >= a.B * a.Hq) return;
   const int b = wid / a.Hq, head = wid % a.Hq;
   const int c0 = a.ws.prefix[b], c1 = a.ws.prefix[b + 1];
@@ -425,6 +428,18 @@ extern "C" size_t vj_paged_decode_workspace_size(int32_t batch, int32_t num_q_he
   return vj::workspace_bytes(batch, num_q_heads, max_chunks);
 }
 
+namespace vj {
+namespace {
+vj_status decode_impl(
+    const void *q, const void *k_cache, const void *v_cache, const int32_t *block_tables,
+    const int32_t *context_lens, void *out, int32_t batch, int32_t num_q_heads,
+    int32_t num_kv_heads, int32_t head_dim, int64_t num_blocks, int32_t block_size,
+    int32_t bt_width, int32_t bt_stride, int64_t stride_block, int64_t stride_token,
+    int64_t stride_head, float scale, int32_t max_chunks, void *workspace,
+    size_t workspace_bytes, cudaStream_t stream, bool plan);
+}  // namespace
+}  // namespace vj
+
 extern "C" vj_status vj_paged_decode(
     const void *q, const void *k_cache, const void *v_cache, const int32_t *block_tables,
     const int32_t *context_lens, void *out, int32_t batch, int32_t num_q_heads,
@@ -432,7 +447,34 @@ extern "C" vj_status vj_paged_decode(
     int32_t bt_width, int32_t bt_stride, int64_t stride_block, int64_t stride_token,
     int64_t stride_head, float scale, int32_t max_chunks, void *workspace,
     size_t workspace_bytes, cudaStream_t stream) {
-  using namespace vj;
+  return vj::decode_impl(q, k_cache, v_cache, block_tables, context_lens, out, batch,
+                         num_q_heads, num_kv_heads, head_dim, num_blocks, block_size, bt_width,
+                         bt_stride, stride_block, stride_token, stride_head, scale, max_chunks,
+                         workspace, workspace_bytes, stream, true);
+}
+
+extern "C" vj_status vj_paged_decode_planned(
+    const void *q, const void *k_cache, const void *v_cache, const int32_t *block_tables,
+    const int32_t *context_lens, void *out, int32_t batch, int32_t num_q_heads,
+    int32_t num_kv_heads, int32_t head_dim, int64_t num_blocks, int32_t block_size,
+    int32_t bt_width, int32_t bt_stride, int64_t stride_block, int64_t stride_token,
+    int64_t stride_head, float scale, int32_t max_chunks, void *workspace,
+    size_t workspace_bytes, cudaStream_t stream) {
+  return vj::decode_impl(q, k_cache, v_cache, block_tables, context_lens, out, batch,
+                         num_q_heads, num_kv_heads, head_dim, num_blocks, block_size, bt_width,
+                         bt_stride, stride_block, stride_token, stride_head, scale, max_chunks,
+                         workspace, workspace_bytes, stream, false);
+}
+
+namespace vj {
+namespace {
+vj_status decode_impl(
+    const void *q, const void *k_cache, const void *v_cache, const int32_t *block_tables,
+    const int32_t *context_lens, void *out, int32_t batch, int32_t num_q_heads,
+    int32_t num_kv_heads, int32_t head_dim, int64_t num_blocks, int32_t block_size,
+    int32_t bt_width, int32_t bt_stride, int64_t stride_block, int64_t stride_token,
+    int64_t stride_head, float scale, int32_t max_chunks, void *workspace,
+    size_t workspace_bytes, cudaStream_t stream, bool plan) {
   if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || num_blocks <= 0 || bt_width < 0 ||
       bt_stride < bt_width) {
     return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_paged_decode: negative or zero size");
@@ -504,10 +546,12 @@ extern "C" vj_status vj_paged_decode(
   a.ws = carve(workspace, batch, num_q_heads, max_chunks);
 
   const int grid = num_sms() * kCtasPerSm;
-  decode_plan_kernel<<<1, 1024, 0, stream>>>(context_lens, batch, num_kv_heads, max_chunks,
-                                             grid * kWarps, a.max_pages, a.ws);
-  rc = check_launch("vj_paged_decode(plan)");
-  if (rc) return rc;
+  if (plan) {
+    decode_plan_kernel<<<1, 1024, 0, stream>>>(context_lens, batch, num_kv_heads, max_chunks,
+                                               grid * kWarps, a.max_pages, a.ws);
+    rc = check_launch("vj_paged_decode(plan)");
+    if (rc) return rc;
+  }
   const size_t smem = smem_bytes();
   cudaFuncSetAttribute(decode_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   decode_chunk_kernel<<<grid, kWarps * 32, smem, stream>>>(tmk, tmv, a);
@@ -517,6 +561,8 @@ extern "C" vj_status vj_paged_decode(
   decode_combine_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(a);
   return check_launch("vj_paged_decode(combine)");
 }
+}  // namespace
+}  // namespace vj
 
 // ---------------------------------------------------------------------------
 // Decode for callers that cannot allocate device memory.

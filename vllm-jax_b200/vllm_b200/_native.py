@@ -36,6 +36,13 @@ PROTOTYPES: dict[str, tuple] = {
         c_i64, c_i64, c_i64,                        # strides
         c_f32, c_i32, c_vp, c_sz, c_vp]),           # scale, max_chunks, ws, ws_bytes, stream
     "vj_paged_decode_noalloc_scratch_bytes": (c_sz, []),
+    "vj_paged_decode_planned": (c_int, [
+        c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,         # q, k_cache, v_cache, bt, lens, out
+        c_i32, c_i32, c_i32, c_i32, c_i64, c_i32,   # B, Hq, Hkv, D, nb, bs
+        c_i32, c_i32,                               # bt_width, bt_stride
+        c_i64, c_i64, c_i64,                        # strides
+        c_f32, c_i32, c_vp, c_sz, c_vp]),           # scale, max_chunks, ws, ws_bytes, stream
+    "vj_paged_decode_noalloc_scratch_bytes": (c_sz, []),
     "vj_paged_decode_noalloc": (c_int, [
         c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,         # q, k_cache, v_cache, bt, lens, out
         c_i32, c_i32, c_i32, c_i32, c_i64, c_i32,   # B, Hq, Hkv, D, nb, bs
@@ -119,7 +126,8 @@ def check(status: int) -> None:
 
 
 # kernels launched by one successful call of each entry point
-KERNELS_PER_CALL = {"vj_paged_decode": 3, "vj_paged_decode_noalloc": 3, "vj_paged_prefill": 2}
+KERNELS_PER_CALL = {"vj_paged_decode": 3, "vj_paged_decode_planned": 2,
+                    "vj_paged_decode_noalloc": 3, "vj_paged_prefill": 2}
 launch_count = 0
 
 

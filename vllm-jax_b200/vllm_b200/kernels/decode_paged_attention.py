@@ -24,7 +24,7 @@ DEFAULT_MASK_VALUE = -0.7 * float(torch.finfo(torch.float32).max)
 
 
 def _launch(q, k_base, v_base, nb, bs, strides, block_tables, lengths, scale, out=None,
-            max_chunks: int = 0, ws: torch.Tensor | None = None):
+            max_chunks: int = 0, ws: torch.Tensor | None = None, reuse_plan: bool = False):
     dev = require_cuda(q, k_base, v_base, block_tables, lengths)
     B, Hq, D = q.shape
     Hkv = strides[3]
@@ -35,7 +35,8 @@ def _launch(q, k_base, v_base, nb, bs, strides, block_tables, lengths, scale, ou
         ws = workspace(dev, ws_bytes, "decode")
     elif ws.numel() < ws_bytes or ws.dtype != torch.uint8:
         raise ValueError(f"decode workspace must be uint8 with >= {ws_bytes} bytes")
-    _native.call("vj_paged_decode", q.data_ptr(), k_base.data_ptr(), v_base.data_ptr(),
+    _native.call("vj_paged_decode_planned" if reuse_plan else "vj_paged_decode",
+                 q.data_ptr(), k_base.data_ptr(), v_base.data_ptr(),
                  block_tables.data_ptr(), lengths.data_ptr(), out.data_ptr(),
                  B, Hq, Hkv, D, nb, bs, block_tables.shape[1], block_tables.stride(0),
                  strides[0], strides[1], strides[2], float(scale), max_chunks,
@@ -98,10 +99,14 @@ def decode_paged_attention(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torc
 def paged_decode(q: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.Tensor,
                  context_lens: torch.Tensor, scale: float | None = None,
                  out: torch.Tensor | None = None, max_chunks: int = 0,
-                 workspace: torch.Tensor | None = None) -> torch.Tensor:
+                 workspace: torch.Tensor | None = None,
+                 reuse_plan: bool = False) -> torch.Tensor:
     """Decode attention straight from the engine cache (2, nb, bs, Hkv, D).
     `workspace` (uint8, decode_workspace_bytes(...) long) pins the split-KV
-    scratch to a caller-owned buffer, as CUDA-graph replays need."""
+    scratch to a caller-owned buffer, as CUDA-graph replays need.
+    `reuse_plan`: skip the planning launch; the workspace must hold the plan of
+    the previous call with the same batch and lengths (the layers of one
+    decode step)."""
     require_dtype(q, torch.bfloat16, "q")
     require_dtype(kv_cache, torch.bfloat16, "kv_cache")
     require_dtype(block_tables, torch.int32, "block_tables")
@@ -119,8 +124,10 @@ def paged_decode(q: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.Te
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     strides = (k.stride(0), k.stride(1), k.stride(2), Hkv)
+    if reuse_plan and workspace is None:
+        raise ValueError("reuse_plan needs the caller's workspace")
     return _launch(q, k, v, nb, bs, strides, block_tables, context_lens, scale, out, max_chunks,
-                   workspace)
+                   workspace, reuse_plan)
 
 
 def decode_workspace_bytes(batch: int, num_q_heads: int, head_dim: int = 128,

@@ -274,10 +274,14 @@ class Qwen3Model:
     def forward_decode(self, meta, kv_caches: list[torch.Tensor]) -> torch.Tensor:
         """One token per row; returns bf16 logits [rows, vocab]."""
         x = self.embed(meta.input_ids)
+        planned = []   # the first layer plans the split; the others reuse it
 
         def attn(q, kv):
-            return paged_decode(q, kv, meta.block_tables, meta.context_lens, self.scale,
-                                workspace=self.decode_workspace)
+            out = paged_decode(q, kv, meta.block_tables, meta.context_lens, self.scale,
+                               workspace=self.decode_workspace,
+                               reuse_plan=bool(planned) and self.decode_workspace is not None)
+            planned.append(True)
+            return out
 
         x = self._stack(x, kv_caches, meta, attn)
         return F.linear(x, self.w.lm_head)           # compute_logits (qwen3.py:474-477)
@@ -291,11 +295,15 @@ class Qwen3Model:
         x = self.embed(meta.input_ids)
         S, nd = meta.num_seqs, num_decode
 
+        planned = []
+
         def attn(q, kv):
             out = torch.empty_like(q)
             if nd:
                 paged_decode(q[:nd], kv, meta.block_tables[:nd], meta.context_lens[:nd],
-                             self.scale, out=out[:nd], workspace=self.decode_workspace)
+                             self.scale, out=out[:nd], workspace=self.decode_workspace,
+                             reuse_plan=bool(planned) and self.decode_workspace is not None)
+                planned.append(True)
             if S > nd:
                 paged_prefill(q, kv, meta.block_tables[nd:S], meta.cu_seqlens_q[nd:S + 1],
                               meta.context_lens[nd:S], max_seqlen_q=meta.max_new,
