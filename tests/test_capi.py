@@ -1,6 +1,5 @@
 """The C-ABI library loads on CPU, exports every symbol include/vjattn.h declares,
 and rejects bad arguments before touching the GPU."""
-import ctypes
 import re
 from pathlib import Path
 

@@ -4,7 +4,6 @@ into Qwen3Weights; at tensor-parallel degree 2 each rank holds exactly the
 rows/columns of its KV heads and intermediate slice
 (vllm/utils/hf_convert.py:30-198 maps the same names)."""
 import json
-import os
 
 import pytest
 import torch

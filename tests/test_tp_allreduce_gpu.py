@@ -7,7 +7,6 @@ order, rounded to bf16, then exactly vj_add_rmsnorm; every rank's result is
 identical. The cross-GPU path is covered by test_tp_nvlink_gpu.py."""
 import ctypes
 
-import numpy as np
 import pytest
 import torch
 
