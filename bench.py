@@ -393,7 +393,7 @@ def run_kvstore(args, rank, world, local_rank):
     row. N > 1: TP by KV head (each rank its heads of every token)."""
     import torch
     import torch.distributed as dist
-    from vllm_b200.kernels.kv_store import kv_store_qknorm_rope
+    from vllm_b200.kernels.kv_store import kv_store_qknorm_rope, rope_table
 
     cfg = C2
     torch.cuda.set_device(local_rank)
@@ -423,9 +423,10 @@ def run_kvstore(args, rank, world, local_rank):
     d_pos = torch.from_numpy(positions).to(dev)
     d_slot = torch.from_numpy(slots).to(dev)
     q_out = torch.empty_like(q)
+    table = rope_table(dev, 1e6, int(positions.max()) + 1)
 
     def step():
-        kv_store_qknorm_rope(q, k, v, kv_cache, d_slot, d_pos, qw, kw, q_out=q_out)
+        kv_store_qknorm_rope(q, k, v, kv_cache, d_slot, d_pos, qw, kw, q_out=q_out, table=table)
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -456,7 +457,8 @@ def run_kvstore(args, rank, world, local_rank):
     def e2e_step():
         for dst, src in ((e_q, h_q), (e_k, h_k), (e_v, h_v), (e_pos, h_pos), (e_slot, h_slot)):
             dst.copy_(src, non_blocking=True)
-        kv_store_qknorm_rope(e_q, e_k, e_v, kv_cache, e_slot, e_pos, qw, kw, q_out=q_out)
+        kv_store_qknorm_rope(e_q, e_k, e_v, kv_cache, e_slot, e_pos, qw, kw, q_out=q_out,
+                             table=table)
         h_out.copy_(q_out, non_blocking=True)
 
     e2e_step()
@@ -505,7 +507,7 @@ def run_kvstore(args, rank, world, local_rank):
                    "l2": f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB per step)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                     "peak_source": f"{peak_src} hbm_gbs", "kernel": "kv_store_qknorm_rope_kernel",
+                     "peak_source": f"{peak_src} hbm_gbs", "kernel": "kv_store_rows_kernel",
                      "traffic": (int(KVSTORE_PROFILE["dram_bytes"] * T / KVSTORE_PROFILE["tokens"])
                                  if world == 1 else None),
                      "traffic_source": "ncu dram bytes of a 16-sequence C2 capture, scaled by "
@@ -705,7 +707,49 @@ def decode_traffic(ctx_tokens: int) -> int:
 # ---------------------------------------------------------------------------
 # reference arm: the reference's algorithm on host CPU cores (oracle port)
 # ---------------------------------------------------------------------------
+def run_reference_e2e(args, rank, world):
+    """C4 output tok/s of the reference's algorithm on the host CPU cores: the
+    oracle restatement of the Qwen3-8B forward, one bounded sample per step
+    (CpuQwen3Sample), scaled to the whole 512-request job."""
+    if rank != 0:
+        return
+    from vllm_b200.model.qwen3 import get_config
+    mcfg = get_config(C4["model"])
+    prompts, outs = c4_requests(C4, mcfg.vocab_size)
+    sample = CpuQwen3Sample(mcfg, prompts, outs)
+    ptoks, otoks = sum(len(p) for p in prompts), sum(outs)
+    for _ in range(args.warmup):
+        sample.measure()
+    vals = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        vals.append(sample.tok_per_s(sample.measure(), ptoks, otoks))
+    wall = time.perf_counter() - t0
+    v = float(np.mean(vals))
+    cores = len(os.sched_getaffinity(0))
+    line = {
+        "impl": "reference", "metric": C4_METRIC, "value": round(v, 4), "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(wall / args.steps * 1e3, 1), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded random token ids and lengths; random-init N(0,0.02) weights)",
+        "config": {"workload": "C4 end-to-end continuous batching", "model": C4["model"],
+                   "num_requests": C4["num_requests"], "output_tokens": otoks,
+                   "prompt_tokens": ptoks, "parallelism": "host CPU cores"},
+        "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": sample.describe(cores)},
+        "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "jax/flax are not installable in this image (no network); the reference's "
+                "forward runs as its NumPy restatement (oracle/), fp32 GEMMs with per-op "
+                "bf16 rounding, on every host core through numpy BLAS.",
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args, rank, world):
+    if args.workload == "e2e":
+        return run_reference_e2e(args, rank, world)
     if rank != 0:
         return
     pool = make_pool()
@@ -743,6 +787,9 @@ def run_reference(args, rank, world):
     pool.terminate()
 
 
+C4_METRIC = ("output tok/s Qwen3-8B continuous batching (C4: 512 requests, prompts "
+             "U[100,1024], outputs U[100,1024])")
+
 # C4: Qwen3-8B continuous batching
 C4 = dict(model="Qwen3-8B", num_requests=512, prompt_min=100, prompt_max=1024, out_min=100,
           out_max=1024, max_num_batched_tokens=16384, max_num_seqs=512, seed=0)
@@ -773,6 +820,89 @@ def c4_requests(cfg=C4, vocab=151936):
     olen = rng.integers(cfg["out_min"], cfg["out_max"] + 1, n)
     prompts = [rng.integers(0, vocab, int(L)).tolist() for L in plen]
     return prompts, [int(x) for x in olen]
+
+
+class CpuQwen3Sample:
+    """A bounded CPU sample of one engine's work at a Qwen3 architecture,
+    run through the oracle's restatement of the reference forward
+    (oracle/qwen3.py: same layer dataflow, bf16 rounding per op, fp32 GEMM
+    accumulation through numpy BLAS on every host core):
+      * one decoder layer of a decode step at `batch` rows whose contexts are
+        drawn from the workload's mid-generation lengths (prompt + U[0, out]),
+      * 1/16 of the lm_head GEMM of those rows,
+      * one decoder layer of a prefill of a median-length prompt.
+    tok_per_s() scales these to the whole job: every output token costs
+    (layers x decode layer + lm_head) / batch and every prompt token layers x
+    prefill layer / prompt length (the reference computes no logits in
+    prefill, model_runner.py:41-59)."""
+
+    def __init__(self, mcfg, prompts, outs, batch=32, seed=0):
+        from types import SimpleNamespace
+
+        from oracle.bf16 import bf16
+        from oracle.qwen3 import OracleQwen3
+        rng = np.random.default_rng(seed)
+        H, I, D = mcfg.hidden_size, mcfg.intermediate_size, mcfg.head_dim
+        Hq, Hkv = mcfg.num_attention_heads, mcfg.num_key_value_heads
+        self.mcfg, self.batch = mcfg, batch
+
+        def w(*shape):
+            return bf16(rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02))
+        one_h, one_d = np.ones(H, np.float32), np.ones(D, np.float32)
+        layer = {"w_qkv": w((Hq + 2 * Hkv) * D, H), "w_o": w(H, Hq * D),
+                 "w_gate_up": w(2 * I, H), "w_down": w(H, I), "ln1": one_h, "ln2": one_h,
+                 "q_norm": one_d, "k_norm": one_d}
+        self.vocab_frac = 16
+        self.lm = w(mcfg.vocab_size // self.vocab_frac, H)
+        pick = rng.choice(len(prompts), size=batch, replace=False)
+        self.ctx = [int(len(prompts[i]) + rng.integers(0, outs[i] + 1)) for i in pick]
+        self.prompt_len = int(np.median([len(p) for p in prompts]))
+        bs = 16
+        nblk = sum((L + bs - 1) // bs for L in self.ctx) + (self.prompt_len + bs - 1) // bs
+        cfg1 = SimpleNamespace(**{**mcfg.__dict__, "num_hidden_layers": 1})
+        self.model = OracleQwen3(cfg1, {"layers": [layer]}, nblk, bs)
+        self.model.kc[0][:] = bf16(rng.standard_normal(self.model.kc[0].shape, dtype=np.float32))
+        self.model.vc[0][:] = bf16(rng.standard_normal(self.model.vc[0].shape, dtype=np.float32))
+        self.tables = np.zeros((batch, max((L + bs - 1) // bs for L in self.ctx)), np.int64)
+        o = 0
+        for i, L in enumerate(self.ctx):
+            n = (L + bs - 1) // bs
+            self.tables[i, :n] = np.arange(o, o + n)
+            o += n
+        self.pre_blocks = np.arange(o, o + (self.prompt_len + bs - 1) // bs)
+        self.x_dec = bf16(rng.standard_normal((batch, H), dtype=np.float32))
+        self.x_pre = bf16(rng.standard_normal((self.prompt_len, H), dtype=np.float32))
+
+    def measure(self):
+        """(decode layer s, full lm_head s, prefill layer s) of one sample."""
+        bs = 16
+        pos = [L - 1 for L in self.ctx]
+        slots = [int(self.tables[i, (L - 1) // bs]) * bs + (L - 1) % bs
+                 for i, L in enumerate(self.ctx)]
+        t0 = time.perf_counter()
+        h = self.model.decode_layers(self.x_dec, pos, slots, self.tables, self.ctx)
+        t1 = time.perf_counter()
+        np.matmul(h, self.lm.T)
+        t2 = time.perf_counter()
+        P = self.prompt_len
+        pslots = [int(self.pre_blocks[t // bs]) * bs + t % bs for t in range(P)]
+        self.model.prefill_layers(self.x_pre, list(range(P)), pslots, [0, P], 1)
+        t3 = time.perf_counter()
+        return t1 - t0, (t2 - t1) * self.vocab_frac, t3 - t2
+
+    def tok_per_s(self, m, prompt_tokens: int, output_tokens: int) -> float:
+        t_dec, t_lm, t_pre = m
+        L = self.mcfg.num_hidden_layers
+        per_out = (L * t_dec + t_lm) / self.batch
+        per_prompt = L * t_pre / self.prompt_len
+        return output_tokens / (output_tokens * per_out + prompt_tokens * per_prompt)
+
+    def describe(self, cores: int) -> str:
+        return (f"oracle.qwen3 restatement of the reference forward on {cores} host cores "
+                f"(numpy BLAS): 1 of {self.mcfg.num_hidden_layers} decoder layers at "
+                f"{self.batch} decode rows (contexts prompt + U[0, out] of sampled requests), "
+                f"1/{self.vocab_frac} of lm_head, 1 layer of a {self.prompt_len}-token prefill; "
+                "scaled to the whole job by layers, rows and tokens")
 
 
 def run_e2e(args, rank, world, local_rank):
@@ -825,62 +955,85 @@ def run_e2e(args, rank, world, local_rank):
     progress(f"engine ready ({eng.config.num_blocks} blocks)")
     eng.runner.capture_all(cfg["max_num_seqs"])
     progress("decode graphs captured" if eng.runner.use_cuda_graphs else "eager decode (TP)")
-    # warm-up: a few short requests (cuBLAS heuristics, prefill kernels)
-    for _ in range(max(args.warmup, 1)):
-        eng.generate(prompts[:8], SamplingParams(temperature=0, max_new_tokens=4,
-                                                 ignore_eos=True))
-    progress("warm-up done")
     params = [SamplingParams(temperature=0, max_new_tokens=o, ignore_eos=True) for o in outs]
-    times, stats = [], []
-    launches0 = _native.launch_count
-    for _ in range(args.steps):
+    stream = torch.cuda.current_stream(dev)
+
+    def one_pass():
+        """One step: generate() over the whole request set. Prompts go host ->
+        device and every step's tokens device -> host inside it."""
         for k in eng.stats:
             eng.stats[k] = 0 if isinstance(eng.stats[k], int) else 0.0
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
-        with ClockSampler(local_rank) as clk:
-            t0 = time.perf_counter()
-            res = eng.generate(prompts, params)
-            torch.cuda.synchronize()
-            t1 = time.perf_counter()
-        times.append(t1 - t0)
-        stats.append(dict(eng.stats))
-        progress(f"timed generate: {t1 - t0:.2f} s")
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        res = eng.generate(prompts, params)
+        e1.record(stream)
+        torch.cuda.synchronize()
         assert [len(r) for r in res] == outs
-    t = torch.tensor([max(times)], dtype=torch.float64, device=dev)
+        return e0.elapsed_time(e1) / 1e3
+
+    for i in range(args.warmup):
+        progress(f"warm-up generate {i + 1}/{args.warmup}: {one_pass():.2f} s")
+    eng.runner.decode_events = []
+    launches0 = _native.launch_count
+    times, stats = [], []
+    with ClockSampler(local_rank) as clk:
+        for i in range(args.steps):
+            times.append(one_pass())
+            stats.append(dict(eng.stats))
+            progress(f"timed generate {i + 1}/{args.steps}: {times[-1]:.2f} s")
+    launches = _native.launch_count - launches0
+    dec_s = sum(a.elapsed_time(b) for a, b in eng.runner.decode_events) / 1e3
+    eng.runner.decode_events = None
+    t = torch.tensor([sum(times)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    wall = float(t.item())
+    total_s = float(t.item())
     eng.close()       # every rank: graphs and the NVLink communicator
     if rank != 0:
         return
-    value = sum(all_outs) / wall
-    st = stats[-1]
+    out_tokens = sum(all_outs)
+    value = out_tokens * args.steps / total_s
     peaks, src = load_peaks()
-    # decode-step roofline: weights of one rank + K/V of every context token per step
+    # decode-step roofline: weights of one rank + K/V of every context token
+    # per decode step, over the CUDA-event time of the decode forwards
     wbytes = sum(p.numel() * 2 for lw in eng.weights.layers for p in
                  (lw.w_qkv, lw.w_o, lw.w_gate_up, lw.w_down)) + eng.weights.lm_head.numel() * 2
     kvb = mcfg.num_hidden_layers * 2 * (mcfg.num_key_value_heads // tp) * mcfg.head_dim * 2
-    dec_bytes = st["decode_steps"] * wbytes + st["decode_ctx_tokens"] * kvb
-    achieved = dec_bytes / max(st["decode_s"], 1e-9) / 1e9
+    dec_steps = sum(st["decode_steps"] for st in stats)
+    dec_ctx = sum(st["decode_ctx_tokens"] for st in stats)
+    achieved = (dec_steps * wbytes + dec_ctx * kvb) / max(dec_s, 1e-9) / 1e9
+    st = stats[-1]
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        sample = CpuQwen3Sample(mcfg, all_prompts, all_outs)
+        sample.measure()                                   # warm the BLAS pools
+        m = [sample.measure() for _ in range(2)]
+        med = tuple(float(np.median([x[j] for x in m])) for j in range(3))
+        cores = len(os.sched_getaffinity(0))
+        cpu = {"value": round(sample.tok_per_s(med, sum(len(p) for p in all_prompts),
+                                               out_tokens), 3),
+               "unit": "tok/s", "cores": cores, "kind": "port",
+               "sample": sample.describe(cores)}
     if c5:
         metric = (f"output tok/s {cfg['model']} continuous batching with chunked prefill (C5: "
                   f"{cfg['num_requests']} requests, prompts clip(lognormal(ln 1024, "
                   f"{cfg['sigma']}), 32, 16384), outputs U[64,2048])")
         workload = "C5 end-to-end, chunked prefill mixed with decode"
     else:
-        metric = (f"output tok/s {cfg['model']} continuous batching (C4: "
-                  f"{cfg['num_requests']} requests, prompts U[100,1024], outputs U[100,1024])")
+        metric = C4_METRIC
         workload = "C4 end-to-end continuous batching"
     line = {
         "metric": metric,
         "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-        "warmup": max(args.warmup, 1), "ms_per_step": round(wall * 1e3, 1),
+        "warmup": args.warmup, "ms_per_step": round(total_s / args.steps * 1e3, 1),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded random token ids and lengths; random-init N(0,0.02) weights)",
         "config": {"workload": workload, "model": cfg["model"],
-                   "num_requests": cfg["num_requests"], "output_tokens": sum(all_outs),
+                   "step": "one Engine.generate() over the whole request set",
+                   "num_requests": cfg["num_requests"], "output_tokens": out_tokens,
                    "prompt_tokens": sum(len(p) for p in all_prompts),
                    "chunked_prefill": c5,
                    "max_num_batched_tokens": cfg["max_num_batched_tokens"],
@@ -888,19 +1041,24 @@ def run_e2e(args, rank, world, local_rank):
                    "parallelism": (f"dp{dp}x" if dp > 1 else "") + f"tp{tp}" if world > 1
                    else "single GPU",
                    "engine_steps": st["steps"], "decode_steps": st["decode_steps"],
-                   "prefill_s": round(st["prefill_s"], 3), "decode_s": round(st["decode_s"], 3),
+                   "decode_s_per_pass": round(dec_s / args.steps, 3),
+                   "timing": "CUDA events around each generate(), max over ranks",
                    "l2": "decode steps stream all weights + KV (> L2)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                      "peak_source": f"{src} hbm_gbs",
-                     "kernel": "decode step (weights/TP + KV bytes per step / host-timed step)",
+                     "kernel": "decode forward (weights of one rank + KV of every context "
+                               "token per step / CUDA-event time of the decode forwards)",
                      "traffic": None},
         "e2e": {"value": round(value, 1), "unit": "tok/s",
-                "h2d_bytes_per_step": st["h2d_bytes"] // max(st["steps"], 1),
-                "d2h_bytes_per_step": st["d2h_bytes"] // max(st["steps"], 1)},
-        "gpu_launches": _native.launch_count - launches0,
+                "h2d_bytes_per_step": st["h2d_bytes"], "d2h_bytes_per_step": st["d2h_bytes"],
+                "note": "the step is the public generate() call itself: prompts are copied "
+                        "host->device and tokens device->host inside every pass"},
+        "gpu_launches": launches,
         "clocks": clk.summary(),
     }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
 
 
@@ -910,8 +1068,11 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "prefill", "kvstore", "e2e", "c5"],
-                    default="decode")
+    ap.add_argument("--workload", choices=["e2e", "decode", "prefill", "kvstore", "c5"],
+                    default="e2e",
+                    help="e2e (default): C4 Qwen3-8B output tok/s, tensor parallel over "
+                         "--gpus; decode: C3 paged decode GB/s; prefill: C2 TFLOP/s; "
+                         "kvstore: K3 GB/s; c5: Qwen3-32B chunked prefill tok/s")
     ap.add_argument("--model", default=None, help="e2e: model preset (default Qwen3-8B)")
     ap.add_argument("--max-num-seqs", type=int, default=None, help="e2e: scheduler seats")
     ap.add_argument("--tp", type=int, default=None,
@@ -951,8 +1112,6 @@ def main():
         elif args.workload == "kvstore":
             run_kvstore(args, rank, world, local_rank)
         elif args.workload in ("e2e", "c5"):
-            if args.steps > 3:
-                args.steps = 1      # one generate() of the whole request set per step
             run_e2e(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)

@@ -62,7 +62,13 @@ enum {
 enum {
   VJ_KV_NORM = 1,          /* apply per-head RMSNorm to q and k (weights required) */
   VJ_KV_ROPE = 2,          /* apply interleaved-pair RoPE to q and k */
-  VJ_KV_WRAP_NEGATIVE = 4  /* slot s<0 writes slot s+num_slots, as JAX .at[] does */
+  VJ_KV_WRAP_NEGATIVE = 4, /* slot s<0 writes slot s+num_slots, as JAX .at[] does */
+  /* q_out = bf16(q / bf16(sqrt(D))): the reference's decode q scaling
+   * (vllm/model/qwen3.py:207); attention then runs with scale 1 */
+  VJ_KV_QSCALE_DIV_SQRT_D = 8,
+  /* q_out = bf16(q * bf16(1/sqrt(D))): the reference's prefill kernel scaling
+   * (vllm/kernels/prefill_paged_attention.py:60); attention then runs with scale 1 */
+  VJ_KV_QSCALE_MUL_RSQRT_D = 16
 };
 
 /* Message of the last failed call on this host thread ("" if none). */
@@ -83,9 +89,14 @@ VJ_API int vj_version(void);
  *   positions [T] int32, slot_mapping [T] int32 (flat slot = block*bs + offset)
  *   q_out [T,Hq,D] bf16 (may equal q_in), k_out [T,Hkv,D] bf16 or NULL
  *   k_cache/v_cache: element (blk,t,h,d) at base + blk*sb + t*st + h*sh + d
+ *   rope_table [rope_table_len][D/2] (cos, sin) bf16 pairs from
+ *   vj_rope_table_build for the same rope_theta; positions outside
+ *   [0, rope_table_len) (or rope_table_len == 0) are computed in the kernel
  * Slots outside [0, num_blocks*block_size) are dropped (after the optional
- * negative wrap). Numerics: sum of squares accumulated in fp64, rounded to
- * fp32; every later step is a correctly rounded fp32 op followed by bf16
+ * negative wrap). Numerics: per row, squares summed in fp32 in a fixed order
+ * (each of the 16 lanes owning dims 8l..8l+7 sums its even and its odd dims
+ * in dim order, adds the two, then a butterfly over lanes xor 8, 4, 2, 1);
+ * every later step is a correctly rounded fp32 op followed by bf16
  * round-to-nearest-even, so the result is reproducible bit for bit.
  * ------------------------------------------------------------------------- */
 VJ_API vj_status vj_kv_store_qknorm_rope(
@@ -97,7 +108,17 @@ VJ_API vj_status vj_kv_store_qknorm_rope(
     int32_t head_dim, int64_t num_blocks, int32_t block_size,
     int64_t stride_block, int64_t stride_token, int64_t stride_head,
     int64_t q_row_stride, int64_t k_row_stride, int64_t v_row_stride,
+    const void *rope_table, int32_t rope_table_len,
     float eps, float rope_theta, int32_t flags, cudaStream_t stream);
+
+/* RoPE table for vj_kv_store_qknorm_rope: for each position p < num_positions
+ * and pair i < D/2, the bf16 word pair (cos, sin) of bf16(bf16(p) *
+ * inv_freq[i]) (vllm/model/qwen3.py:62-67), inv_freq in bf16 from the bf16
+ * rope_theta. Built once per model (positions repeat across layers and steps);
+ * the caller allocates vj_rope_table_bytes() bytes, 16-byte aligned. */
+VJ_API size_t vj_rope_table_bytes(int32_t num_positions, int32_t head_dim);
+VJ_API vj_status vj_rope_table_build(void *table, int32_t num_positions, int32_t head_dim,
+                                     float rope_theta, cudaStream_t stream);
 
 /* ---------------------------------------------------------------------------
  * K2: split-KV paged decode attention (one query token per sequence).

@@ -6,7 +6,9 @@ Follows vllm-jax vllm/model/qwen3.py:
             (x[0::2], x[1::2]); stack((x1*cos - x2*sin, x1*sin + x2*cos), -1)
   :105-111  _update_kv_cache: flat_cache.at[0|1, slot].set(k|v, mode="drop")
 RMSNorm follows flax nnx.RMSNorm (flax 0.12.2, call sites qwen3.py:248-268):
-fp32 statistics, y = bf16(x * (rsqrt(mean(x^2) + eps) * scale)).
+fp32 statistics, y = bf16(x * (rsqrt(mean(x^2) + eps) * scale)). rmsnorm()
+(hidden-size rows) takes the sum of squares exactly (fp64, then fp32);
+rmsnorm_head() (the 128-dim q/k rows of K3) sums in fp32 in K3's order.
 
 Every step below is one IEEE fp32 (or fp64 where stated) operation followed
 by a bf16 round-to-nearest-even wherever jnp's result dtype is bf16, so the
@@ -49,6 +51,46 @@ def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
     return bf16((x * mul).astype(np.float32))
 
 
+def rmsnorm_head(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """flax RMSNorm over a 128-dim head row with the sum of squares taken in
+    fp32 in the order vj_kv_store_qknorm_rope uses: lane l of 16 owns dims
+    8l..8l+7 and sums its even dims and its odd dims in dim order, adds the
+    two, then lanes combine by a butterfly (xor 8, 4, 2, 1). bf16 squares are
+    exact in fp32, so only the order of the additions is a choice (XLA's
+    reduction order is not observable here)."""
+    x = np.asarray(x, np.float32)
+    D = x.shape[-1]
+    sq = (x * x).reshape(*x.shape[:-1], D // 8, 8)
+    se = sq[..., 0]
+    so = sq[..., 1]
+    for j in (2, 4, 6):
+        se = (se + sq[..., j]).astype(np.float32)
+        so = (so + sq[..., j + 1]).astype(np.float32)
+    lane = (se + so).astype(np.float32)
+    idx = np.arange(D // 8)
+    for o in (8, 4, 2, 1):
+        lane = (lane + lane[..., idx ^ o]).astype(np.float32)
+    ss = lane[..., :1]
+    ms = (ss * np.float32(1.0 / D)).astype(np.float32)
+    inv = (np.float32(1.0) / np.sqrt((ms + np.float32(eps)).astype(np.float32))).astype(np.float32)
+    mul = (inv * np.asarray(w, np.float32)).astype(np.float32)
+    return bf16((x * mul).astype(np.float32))
+
+
+def scale_q(q: np.ndarray, mode: str | None) -> np.ndarray:
+    """The reference's bf16 q scalings: "div" = bf16(q / bf16(sqrt(D)))
+    (decode, qwen3.py:207), "mul" = bf16(q * bf16(1/sqrt(D))) (prefill kernel,
+    prefill_paged_attention.py:60); None leaves q unchanged."""
+    if mode is None:
+        return q
+    D = q.shape[-1]
+    if mode == "div":
+        return bf16(q / np.float32(bf16(np.float32(np.sqrt(np.float32(D))))))
+    if mode == "mul":
+        return bf16(q * np.float32(bf16(np.float32(1.0 / np.sqrt(D)))))
+    raise ValueError(f"unknown q scaling {mode!r}")
+
+
 def apply_rope(x: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
     """Interleaved-pair RoPE of qwen3.py:69-75, bf16 after every op. x [T, H, D]."""
     x1 = x[..., 0::2]
@@ -87,17 +129,19 @@ def update_kv_cache(k_cache: np.ndarray, v_cache: np.ndarray, slot_mapping: np.n
 
 def kv_store_qknorm_rope(q, k, v, q_norm_w, k_norm_w, positions, slot_mapping,
                          k_cache, v_cache, eps=1e-6, rope_theta=1e6,
-                         norm=True, rope=True, wrap_negative=True):
-    """Oracle of vj_kv_store_qknorm_rope. Returns (q_out, k_out); updates caches."""
+                         norm=True, rope=True, wrap_negative=True, q_scale=None):
+    """Oracle of vj_kv_store_qknorm_rope. Returns (q_out, k_out); updates caches.
+    q_scale: None, "div" (VJ_KV_QSCALE_DIV_SQRT_D) or "mul" (VJ_KV_QSCALE_MUL_RSQRT_D)."""
     q = np.asarray(q, np.float32)
     k = np.asarray(k, np.float32)
     if norm:
-        q = rmsnorm(q, q_norm_w, eps)
-        k = rmsnorm(k, k_norm_w, eps)
+        q = rmsnorm_head(q, q_norm_w, eps)
+        k = rmsnorm_head(k, k_norm_w, eps)
     if rope:
-        c, s = rope_cos_sin(positions, rope_theta, q.shape[-1])
+        c, s = rope_cos_sin(positions, rope_theta, k.shape[-1])
         q = apply_rope(q, c, s)
         k = apply_rope(k, c, s)
+    q = scale_q(q, q_scale)
     update_kv_cache(k_cache, v_cache, slot_mapping, k, np.asarray(v, np.float32),
                     wrap_negative)
     return q, k

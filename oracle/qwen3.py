@@ -76,6 +76,11 @@ class OracleQwen3:
         return bf16(x + _mm(m, lw["w_down"]))
 
     def prefill(self, ids, positions, slots, cu, num_seqs):
+        x = bf16(self.W["embed"][np.asarray(ids)])
+        return self.prefill_layers(x, positions, slots, cu, num_seqs)
+
+    def prefill_layers(self, x, positions, slots, cu, num_seqs, layers=None):
+        """The decoder layers of a packed prefill on hidden states x [T, hidden]."""
         c = self.cfg
         D = c.head_dim
         g = c.num_attention_heads // c.num_key_value_heads
@@ -99,12 +104,20 @@ class OracleQwen3:
                 out[a:b] = bf16(o.transpose(2, 0, 1, 3).reshape(n, -1, D))
             return out
 
-        x = bf16(self.W["embed"][np.asarray(ids)])
-        for l in range(c.num_hidden_layers):
+        for l in range(c.num_hidden_layers if layers is None else layers):
             x = self._layer(l, x, positions, slots, attn)
         return x
 
     def decode(self, ids, positions, slots, block_tables, ctx):
+        c = self.cfg
+        x = bf16(self.W["embed"][np.asarray(ids)])
+        x = self.decode_layers(x, positions, slots, block_tables, ctx)
+        x = okv.rmsnorm(x, self.W["norm"], c.rms_norm_eps)
+        return _mm(x, self.W["lm_head"])
+
+    def decode_layers(self, x, positions, slots, block_tables, ctx, layers=None):
+        """The decoder layers of a decode step on hidden states x [B, hidden]
+        (all layers, or the first `layers`)."""
         c = self.cfg
         D = c.head_dim
         g = c.num_attention_heads // c.num_key_value_heads
@@ -124,11 +137,9 @@ class OracleQwen3:
                 out[b] = bf16(o.reshape(-1, D))
             return out
 
-        x = bf16(self.W["embed"][np.asarray(ids)])
-        for l in range(c.num_hidden_layers):
+        for l in range(c.num_hidden_layers if layers is None else layers):
             x = self._layer(l, x, positions, slots, attn)
-        x = okv.rmsnorm(x, self.W["norm"], c.rms_norm_eps)
-        return _mm(x, self.W["lm_head"])
+        return x
 
 
 def _mixed_attn(model, starts, ns, tables):
@@ -210,11 +221,16 @@ def greedy_replay_chunked(model: OracleQwen3, trace: list, prompts: list[list[in
     return tokens, gaps
 
 
-def greedy_replay(model: OracleQwen3, trace: dict, prompts: list[list[int]]):
+def greedy_replay(model: OracleQwen3, trace: dict, prompts: list[list[int]],
+                  forced: dict[int, list[int]] | list[list[int]] | None = None):
     """Replay the scheduled steps of a golden host trace (block tables, slots
-    and positions depend only on lengths there) with the oracle's own tokens.
-    Returns (tokens per request id, per decode step a list of (top id, top
-    logit, top-2 logit gap) per scheduled row)."""
+    and positions depend only on lengths there). Without `forced` the oracle
+    feeds back its own argmax; with `forced` (completion tokens per request,
+    e.g. another engine's output) it feeds those instead, so every step of
+    that engine can be checked against the oracle's logits for the same
+    history. Returns (tokens per request id, per decode step a list of (top
+    id, top logit, top-2 logit gap, logit of the token fed back) per
+    scheduled row)."""
     tokens = {i: list(p) for i, p in enumerate(prompts)}
     gaps = []
     for st in trace["steps"]:
@@ -229,8 +245,11 @@ def greedy_replay(model: OracleQwen3, trace: dict, prompts: list[list[int]]):
                 lg = logits[row]
                 top = int(np.argmax(lg))
                 srt = np.sort(lg)
-                step.append((top, float(srt[-1]), float(srt[-1] - srt[-2])))
-                tokens[r].append(top)
+                nxt = top
+                if forced is not None:
+                    nxt = int(forced[r][len(tokens[r]) - len(prompts[r])])
+                step.append((top, float(srt[-1]), float(srt[-1] - srt[-2]), float(lg[nxt])))
+                tokens[r].append(nxt)
             gaps.append(step)
         if "prefill" in st:
             p = st["prefill"]

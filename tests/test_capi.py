@@ -34,13 +34,28 @@ def test_library_exports_every_declared_symbol():
 def test_validation_without_gpu():
     from vllm_b200 import _native
     lib = _native.load()
-    assert lib.vj_version() >> 16 == 1
+    assert lib.vj_version() >> 16 == 2
     # head_dim 64 is rejected before any CUDA call
     st = lib.vj_kv_store_qknorm_rope(None, 1, 1, None, None, None, 1, None, None, 16, 16,
-                                     4, 0, 2, 64, 4, 16, 4096, 256, 128, 0, 0, 0, 1e-6, 1e6, 0,
-                                     None)
+                                     4, 0, 2, 64, 4, 16, 4096, 256, 128, 0, 0, 0, None, 0,
+                                     1e-6, 1e6, 0, None)
     assert st == _native.VJ_ERR_UNSUPPORTED
     assert b"head_dim" in lib.vj_get_last_error()
+    # both q scalings at once are rejected
+    st = lib.vj_kv_store_qknorm_rope(None, 1, 1, None, None, None, 1, None, None, 16, 16,
+                                     4, 0, 2, 128, 4, 16, 4096, 256, 128, 0, 0, 0, None, 0,
+                                     1e-6, 1e6, _native.VJ_KV_QSCALE_DIV_SQRT_D
+                                     | _native.VJ_KV_QSCALE_MUL_RSQRT_D, None)
+    assert st == _native.VJ_ERR_INVALID_ARGUMENT
+    # a misaligned rope table is rejected
+    st = lib.vj_kv_store_qknorm_rope(None, 16, 16, None, None, 16, 16, None, None, 16, 16,
+                                     4, 0, 2, 128, 4, 16, 4096, 256, 128, 0, 0, 0, 8, 10,
+                                     1e-6, 1e6, _native.VJ_KV_ROPE, None)
+    assert st == _native.VJ_ERR_INVALID_ARGUMENT
+    assert b"rope_table" in lib.vj_get_last_error()
+    assert lib.vj_rope_table_bytes(1000, 128) == 1000 * 64 * 4
+    assert lib.vj_rope_table_bytes(1000, 64) == 0
+    assert lib.vj_rope_table_build(None, 10, 128, 1e6, None) == _native.VJ_ERR_INVALID_ARGUMENT
     st = lib.vj_paged_decode(1, 1, 1, 1, 1, 1, 2, 12, 8, 128, 10, 16, 4, 4, 16 * 1024, 1024,
                              128, 0.1, 0, None, 0, None)
     assert st == _native.VJ_ERR_INVALID_ARGUMENT

@@ -48,37 +48,53 @@ def test_c1_engine_runs_and_schedules_like_reference(c1_run):
     assert [b.block_id for b in eng.kv.free_block_queue] == sc["steps"][-1]["free_blocks"]
 
 
+def _bf16_ulp(x: float) -> float:
+    return 2.0 ** (math.floor(math.log2(max(abs(x), 2.0 ** -10))) - 7)
+
+
 def test_c1_greedy_tokens_vs_oracle(c1_run):
-    """Greedy tokens of the first 32 steps against the oracle's restatement of
-    the reference forward. Logits are bf16, so a top-2 gap of a few ulps can
-    flip argmax under any change of accumulation order; a divergence is only
-    accepted at such a near-tie, and the run must agree step for step until it."""
+    """Greedy tokens of the first 32 steps of all 4 C1 requests against the
+    oracle's restatement of the reference forward (bf16 q scaling as the
+    reference, compat=True).
+
+    Every one of the 4 x 32 steps is checked: the oracle replays the ENGINE's
+    tokens (teacher forcing) and at each step the engine's token must be the
+    oracle's argmax, or -- logits are bf16, so accumulation order can move a
+    logit by an ulp -- within 2 bf16 ulps of the oracle's top logit (a near
+    tie). The free-running agreement (oracle feeding back its own argmax) is
+    reported too."""
     from oracle.qwen3 import OracleQwen3, greedy_replay
     sc, cfg, weights, eng, outs = c1_run
-    model = OracleQwen3(cfg, weights.full_numpy(), sc["config"]["num_blocks"],
-                        sc["config"]["block_size"])
-    tokens, gaps = greedy_replay(model, sc, sc["prompts"])
-    n_match, first_div = 0, None
+    W = weights.full_numpy()
+    nb, bs = sc["config"]["num_blocks"], sc["config"]["block_size"]
+    _, steps = greedy_replay(OracleQwen3(cfg, W, nb, bs), sc, sc["prompts"], forced=outs)
+    n_rows = sum(len(s) for s in steps)
+    assert n_rows == 4 * 32
+    seen = {r: 0 for r in range(4)}
+    identical, ties = 0, []
+    for st, step in zip((s for s in sc["steps"] if "decode" in s), steps):
+        for r, (top, top_logit, gap, chosen) in zip(st["decode_ids"], step):
+            k = seen[r]
+            seen[r] += 1
+            if outs[r][k] == top:
+                identical += 1
+                continue
+            deficit = top_logit - chosen
+            ties.append((r, k, deficit / _bf16_ulp(top_logit)))
+            assert deficit <= 2 * _bf16_ulp(top_logit) + 1e-9, (
+                f"request {r} step {k}: engine token {outs[r][k]} is {deficit:.5f} below the "
+                f"oracle's top logit {top_logit:.4f} (top {top})")
+    free, _ = greedy_replay(OracleQwen3(cfg, W, nb, bs), sc, sc["prompts"])
+    prefix = []
     for r in range(4):
-        ref = tokens[r][len(sc["prompts"][r]):]
-        got = outs[r]
-        for step, (a, b) in enumerate(zip(got, ref)):
-            if a != b:
-                if first_div is None or step < first_div[1]:
-                    first_div = (r, step)
-                break
-            n_match += 1
-    print(f"greedy agreement: {n_match}/128 tokens before the first divergence per request; "
-          f"first divergence {first_div}")
-    if first_div is not None:
-        r, step = first_div
-        _, top_logit, gap = gaps[step][r]
-        # a few bf16 ulps at the magnitude of the top logit (logits are bf16)
-        ulp = 2.0 ** (math.floor(math.log2(max(abs(top_logit), 2.0 ** -10))) - 7)
-        print(f"oracle top logit {top_logit:.4f}, top-2 gap {gap:.4f} ({gap / ulp:.1f} ulp)")
-        assert gap <= 4 * ulp + 1e-9, (
-            f"request {r} diverged at step {step} with an oracle top-2 gap of {gap}")
-    assert n_match >= 64
+        ref = free[r][len(sc["prompts"][r]):]
+        n = 0
+        while n < 32 and outs[r][n] == ref[n]:
+            n += 1
+        prefix.append(n)
+    print(f"greedy parity: {identical}/128 steps pick the oracle's argmax; near ties "
+          f"(request, step, ulps below the top): {ties}; free-running identical prefix per "
+          f"request: {prefix} (sum {sum(prefix)}/128)")
 
 
 def test_attention_boundary_reference_signature():

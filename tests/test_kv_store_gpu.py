@@ -39,6 +39,48 @@ def _case(T, Hq, Hkv, nb, bs, seed, pos_max=40000, neg_slots=0, dup_slots=False)
     return q, k, v, qw, kw, pos, slots, cache
 
 
+@pytest.mark.parametrize("q_scale", [None, "div", "mul"])
+@pytest.mark.parametrize("table_positions", [0, 100, 50000])
+def test_kv_store_q_scaling_and_rope_table(q_scale, table_positions):
+    """The reference's bf16 q scalings, and positions inside / past the end of
+    the (cos, sin) table (past the end: computed in the kernel, same bits)."""
+    from vllm_b200.kernels.kv_store import kv_store_qknorm_rope, rope_table
+    q, k, v, qw, kw, pos, slots, cache = _case(257, 32, 8, 32, 16, seed=5, pos_max=45000)
+    kc, vc = cache[0].copy(), cache[1].copy()
+    q_ref, k_ref = ork.kv_store_qknorm_rope(q, k, v, qw, kw, pos, slots, kc, vc,
+                                            eps=1e-6, rope_theta=1e6, q_scale=q_scale)
+    dcache = _bf16_tensor(cache)
+    table = None
+    if table_positions:
+        table = rope_table(torch.device("cuda"), 1e6, table_positions)[:table_positions * 64]
+    else:
+        table = torch.empty(0, dtype=torch.int32, device="cuda")
+    q_out, k_out = kv_store_qknorm_rope(_bf16_tensor(q), _bf16_tensor(k), _bf16_tensor(v),
+                                        dcache, torch.from_numpy(slots).cuda(),
+                                        torch.from_numpy(pos).cuda(), _bf16_tensor(qw),
+                                        _bf16_tensor(kw), eps=1e-6, rope_theta=1e6,
+                                        return_k=True, q_scale=q_scale, table=table)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(_np(q_out), q_ref)
+    np.testing.assert_array_equal(_np(k_out), k_ref)
+    got = _np(dcache)
+    np.testing.assert_array_equal(got[0], kc)
+    np.testing.assert_array_equal(got[1], vc)
+
+
+def test_rope_table_matches_oracle():
+    from vllm_b200.kernels.kv_store import rope_table
+    n = 70000
+    tab = rope_table(torch.device("cuda"), 1e6, n)[:n * 64].view(n, 64).cpu().numpy()
+    pos = np.arange(n, dtype=np.int32)
+    c, s = ork.rope_cos_sin(pos, 1e6)
+    words = tab.view(np.uint32)
+    got_c = (words & 0xFFFF).astype(np.uint32) << 16
+    got_s = words & 0xFFFF0000
+    np.testing.assert_array_equal(got_c.view(np.float32), c)
+    np.testing.assert_array_equal(got_s.view(np.float32), s)
+
+
 @pytest.mark.parametrize("T,Hq,Hkv,nb,bs,neg", [
     (1, 16, 8, 4, 16, 0),
     (37, 16, 8, 8, 16, 3),        # 0.6B heads, padded tokens with slot -1

@@ -6,38 +6,109 @@
 //   vllm/model/qwen3.py:59-78    apply_rope (positions and inv_freq in bf16,
 //                                pairs (x[2i], x[2i+1]), bf16 cos/sin)
 //   vllm/model/qwen3.py:105-111  _update_kv_cache (.at[slot].set, mode=drop)
+//   vllm/model/qwen3.py:207      decode q scaling q / bf16(sqrt(D)) (flag)
+//   vllm/kernels/prefill_paged_attention.py:60  prefill q * bf16(1/sqrt(D)) (flag)
 //
-// Work split: a CTA owns one token. Every half-warp first issues the 16-byte
-// loads of all its (head) rows of that token, so the loads are in flight
-// together, while the first 64 threads compute the token's bf16 cos/sin pairs
-// (fp64 trig, rounded once to bf16) into shared memory; then each half-warp
-// normalises, rotates and stores its rows: 16 lanes x 16 bytes = one 128-dim
-// head row, every global access a coalesced 16-byte vector.
-// HBM-bound: each input byte is read once and each output byte written once.
+// Work split: the launch's (token, head) rows are numbered token-major, and a
+// 256-thread CTA takes 64 consecutive rows per step (a grid-stride loop), so
+// every CTA is full whatever the head count (48 rows per token at Qwen3-8B,
+// 6 at its TP-8 shard). A half-warp owns one 128-dim row: 16 lanes x 16 bytes,
+// every global access a coalesced 16-byte vector. Each half-warp first issues
+// the loads of its 4 rows (and their positions and slots), then the 16-byte
+// reads of their cos/sin pairs from a per-position table (vj_rope_table_build:
+// 256 B per position, L2-resident), then computes and stores.
+//
+// Arithmetic per q/k element (the kernel is HBM-bound only if it issues few
+// instructions per byte): squares with packed fma.rn.f32x2, norm scale
+// products with mul.rn.f32x2, one cvt.rn.bf16x2 per pair, and RoPE as two
+// mul.rn.bf16x2 (x1*cos, x2*sin | x1*sin, x2*cos), two byte permutes and one
+// fma.rn.bf16x2 by (-1, +1). bf16 products and sums rounded once in bf16 equal
+// the reference's fp32-op-then-round-to-bf16 (24 >= 2*8+2 bits: double
+// rounding is innocuous for +, -, *), so every output is bit-reproducible.
 #include "../../include/vjattn.h"
 #include "vj_common.cuh"
 
+#include <algorithm>
 #include <cmath>
 #include <string>
 
 namespace vj {
 namespace {
 
-constexpr int kThreads = 256;   // 16 half-warps
+constexpr int kThreads = 256;      // 16 half-warps
 constexpr int kHeadDim = 128;
 constexpr int kPairs = kHeadDim / 2;
-constexpr int kRowsPerHw = 6;   // rows in flight per half-warp (96 heads per pass)
-
-// Elementwise product of two bf16x2 words, each lane rounded to nearest even.
-__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
+constexpr int kRowsPerHw = 4;      // rows in flight per half-warp
+constexpr int kRowsPerCta = 16 * kRowsPerHw;
+// bf16x2 word (lo = -1.0, hi = +1.0)
+constexpr uint32_t kMinusPlusOne = 0x3F80BF80u;
+// bf16(1/sqrt(128)) in both halves (prefill_paged_attention.py:60)
+constexpr uint32_t kRsqrtDx2 = 0x3DB53DB5u;
 
 struct RopeTable {
   float inv_freq[kPairs];  // bf16-valued
 };
+
+struct KvArgs {
+  const __nv_bfloat16 *q_in, *k_in, *v_in;
+  const __nv_bfloat16 *q_w, *k_w;
+  const int32_t *positions, *slots;
+  __nv_bfloat16 *q_out, *k_out, *k_cache, *v_cache;
+  const uint4 *rope_table;   // [table_len][16] uint4: 4 (cos,sin) bf16x2 words per lane
+  int64_t t_begin;           // first token of this launch
+  uint32_t num_rows;         // rows of this launch (tokens * heads)
+  uint32_t heads_magic;      // floor(2^32 / heads) + 1
+  int Hq, Hkv, heads;
+  int table_len;
+  int64_t num_slots;
+  int block_size, bs_shift;  // bs_shift >= 0 when block_size is a power of two
+  int64_t sb, st, sh, qrs, krs, vrs;
+  float eps;
+  int flags;
+  RopeTable rope;
+};
+
+VJ_DEV uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+VJ_DEV uint32_t bf16x2_fma(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+VJ_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+VJ_DEV uint64_t f32x2(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+VJ_DEV void f32x2_split(uint64_t v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+VJ_DEV uint64_t f32x2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+VJ_DEV uint64_t f32x2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// (lo, hi) f32 -> bf16x2 word, round to nearest even
+VJ_DEV uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+// bf16x2 word -> f32x2 (lo, hi)
+VJ_DEV uint64_t unpack_f32x2(uint32_t w) { return f32x2(bf16_lo(w), bf16_hi(w)); }
 
 // Round a double to the nearest bf16 (ties to even) in one step.
 __host__ __device__ inline float bf16_from_f64(double x) {
@@ -59,122 +130,177 @@ __host__ __device__ inline float bf16_from_f64(double x) {
   return static_cast<float>(r);  // exact: r has 8 significant bits
 }
 
+// (cos, sin) of pair i at `position` as one bf16x2 word (lo = cos, hi = sin):
+// positions.astype(bf16), freqs = bf16(pos * inv_freq) (qwen3.py:62-65), trig
+// in fp64 rounded once to bf16.
+__device__ __noinline__ uint32_t rope_word(int position, float inv_freq) {
+  const float pos = round_bf16(static_cast<float>(position));
+  const float f = round_bf16(pos * inv_freq);
+  double s, c;
+  sincos(static_cast<double>(f), &s, &c);
+  return pack_bf16(bf16_from_f64(c), bf16_from_f64(s));  // exact: bf16 values
+}
+
 __global__ void __launch_bounds__(kThreads)
-kv_store_qknorm_rope_kernel(const __nv_bfloat16 *__restrict__ q_in,
-                            const __nv_bfloat16 *__restrict__ k_in,
-                            const __nv_bfloat16 *__restrict__ v_in,
-                            const __nv_bfloat16 *__restrict__ q_w,
-                            const __nv_bfloat16 *__restrict__ k_w,
-                            const int32_t *__restrict__ positions,
-                            const int32_t *__restrict__ slots,
-                            __nv_bfloat16 *q_out, __nv_bfloat16 *k_out,
-                            __nv_bfloat16 *k_cache, __nv_bfloat16 *v_cache,
-                            int64_t T, int Hq, int Hkv, int64_t num_slots,
-                            int block_size, int64_t sb, int64_t st, int64_t sh,
-                            int64_t qrs, int64_t krs, int64_t vrs,
-                            float eps, int flags, RopeTable rope) {
-  // per pair: bf16x2 words (cos, sin) and (sin, cos)
-  __shared__ uint2 cs[kPairs];
-  const int64_t t = blockIdx.x;
+rope_table_kernel(uint32_t *table, int num_positions, RopeTable rope) {
+  const int64_t n = static_cast<int64_t>(num_positions) * kPairs;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    table[i] = rope_word(static_cast<int>(i / kPairs), rope.inv_freq[i % kPairs]);
+  }
+}
+
+// Norm (optional) + RoPE (optional) + q scaling (optional) of one 8-element
+// lane slice `wd` of a q or k row.
+VJ_DEV void norm_rope_slice(uint32_t (&wd)[4], const uint32_t (&w)[4], const uint4 &tab,
+                            uint32_t half_mask, float eps, bool do_norm, bool do_rope,
+                            int qscale) {
+  if (do_norm) {
+    uint64_t xp[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) xp[j] = unpack_f32x2(wd[j]);
+    // per lane: (sum of even dims, sum of odd dims) in dim order, in fp32
+    uint64_t s2 = f32x2_mul(xp[0], xp[0]);
+#pragma unroll
+    for (int j = 1; j < 4; ++j) s2 = f32x2_fma(xp[j], xp[j], s2);
+    float se, so;
+    f32x2_split(s2, se, so);
+    float ss = __fadd_rn(se, so);
+    // butterfly over the half-warp's 16 lanes (its two halves may hold rows
+    // of different kinds, so the mask is the half-warp)
+#pragma unroll
+    for (int o = 8; o >= 1; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(half_mask, ss, o));
+    // flax RMSNorm: y = bf16(x * (rsqrt(mean(x^2) + eps) * scale)); mean = sum / 128
+    // is a power-of-two scale, exact as a multiply
+    const float ms = __fmul_rn(ss, 1.0f / kHeadDim);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+    const uint64_t inv2 = f32x2(inv, inv);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint64_t m = f32x2_mul(inv2, unpack_f32x2(w[j]));
+      float y0, y1;
+      f32x2_split(f32x2_mul(xp[j], m), y0, y1);
+      wd[j] = cvt_bf16x2(y0, y1);
+    }
+  }
+  if (do_rope) {
+    const uint32_t cs[4] = {tab.x, tab.y, tab.z, tab.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      // pair (x1, x2) = word j; stack((x1*cos - x2*sin, x1*sin + x2*cos), -1)
+      const uint32_t p = bf16x2_mul(wd[j], cs[j]);                     // (x1 c, x2 s)
+      const uint32_t q = bf16x2_mul(wd[j], prmt(cs[j], cs[j], 0x1032)); // (x1 s, x2 c)
+      const uint32_t u = prmt(p, q, 0x5410);                           // (x1 c, x1 s)
+      const uint32_t v = prmt(p, q, 0x7632);                           // (x2 s, x2 c)
+      wd[j] = bf16x2_fma(v, kMinusPlusOne, u);
+    }
+  }
+  if (qscale == VJ_KV_QSCALE_MUL_RSQRT_D) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) wd[j] = bf16x2_mul(wd[j], kRsqrtDx2);
+  } else if (qscale == VJ_KV_QSCALE_DIV_SQRT_D) {
+    // bf16(x / 11.3125) for every bf16 x equals bf16(fp32(x * fp32(1/11.3125)))
+    // (checked exhaustively over all finite bf16 values)
+    const uint64_t r2 = f32x2(1.0f / 11.3125f, 1.0f / 11.3125f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float y0, y1;
+      f32x2_split(f32x2_mul(unpack_f32x2(wd[j]), r2), y0, y1);
+      wd[j] = cvt_bf16x2(y0, y1);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 3)
+kv_store_rows_kernel(const KvArgs a) {
   const int tid = threadIdx.x;
-  const bool do_norm = (flags & VJ_KV_NORM) != 0;
-  const bool do_rope = (flags & VJ_KV_ROPE) != 0;
-  const int heads = Hq + 2 * Hkv;
   const int hw = tid >> 4;     // half-warp index
   const int l16 = tid & 15;    // lane inside the half-warp: dims 8*l16 .. +7
-  int64_t slot = slots[t];
-  if (slot < 0 && (flags & VJ_KV_WRAP_NEGATIVE)) slot += num_slots;
+  const unsigned half_mask = 0xffffu << (16 * (hw & 1));
+  const bool do_norm = (a.flags & VJ_KV_NORM) != 0;
+  const bool do_rope = (a.flags & VJ_KV_ROPE) != 0;
+  const int qscale = a.flags & (VJ_KV_QSCALE_DIV_SQRT_D | VJ_KV_QSCALE_MUL_RSQRT_D);
+  uint32_t qw[4] = {0u, 0u, 0u, 0u}, kw[4] = {0u, 0u, 0u, 0u};
+  if (do_norm) {
+    if (a.Hq > 0) {
+      const uint4 t = __ldg(reinterpret_cast<const uint4 *>(a.q_w + l16 * 8));
+      qw[0] = t.x; qw[1] = t.y; qw[2] = t.z; qw[3] = t.w;
+    }
+    const uint4 t = __ldg(reinterpret_cast<const uint4 *>(a.k_w + l16 * 8));
+    kw[0] = t.x; kw[1] = t.y; kw[2] = t.z; kw[3] = t.w;
+  }
 
-  for (int base = 0; base < heads; base += 16 * kRowsPerHw) {
-    // ---- 1. loads of this half-warp's rows, all in flight together
-    uint4 raw[kRowsPerHw];
+  for (uint32_t base = blockIdx.x * kRowsPerCta; base < a.num_rows;
+       base += gridDim.x * kRowsPerCta) {
+    uint4 raw[kRowsPerHw], tab[kRowsPerHw];
+    int tok[kRowsPerHw], head[kRowsPerHw], pos[kRowsPerHw];
+    // ---- 1. indices, the rows' loads and positions, all in flight together
 #pragma unroll
     for (int k = 0; k < kRowsPerHw; ++k) {
-      const int hidx = base + hw + 16 * k;
+      const uint32_t r = base + hw + 16 * k;
       raw[k] = make_uint4(0u, 0u, 0u, 0u);
-      if (hidx < heads) {
+      tab[k] = make_uint4(0u, 0u, 0u, 0u);
+      tok[k] = -1;
+      head[k] = 0;
+      pos[k] = 0;
+      if (r < a.num_rows) {
+        const uint32_t tl = __umulhi(r, a.heads_magic);   // r / heads (host-checked range)
+        const int h = static_cast<int>(r - tl * a.heads);
+        const int64_t t = a.t_begin + tl;
+        tok[k] = static_cast<int>(tl);
+        head[k] = h;
         const __nv_bfloat16 *src =
-            hidx < Hq ? q_in + t * qrs + hidx * kHeadDim
-            : hidx < Hq + Hkv ? k_in + t * krs + (hidx - Hq) * kHeadDim
-                              : v_in + t * vrs + (hidx - Hq - Hkv) * kHeadDim;
-        raw[k] = *reinterpret_cast<const uint4 *>(src + l16 * 8);
+            h < a.Hq ? a.q_in + t * a.qrs + h * kHeadDim
+            : h < a.Hq + a.Hkv ? a.k_in + t * a.krs + (h - a.Hq) * kHeadDim
+                               : a.v_in + t * a.vrs + (h - a.Hq - a.Hkv) * kHeadDim;
+        raw[k] = __ldcs(reinterpret_cast<const uint4 *>(src + l16 * 8));
+        if (do_rope && h < a.Hq + a.Hkv) pos[k] = __ldg(a.positions + t);
       }
     }
-    // ---- 2. the token's cos/sin (first pass only)
-    if (base == 0 && do_rope) {
-      if (tid < kPairs) {
-        // positions.astype(bf16); freqs = bf16(pos * inv_freq)  (qwen3.py:62-65)
-        const float pos = round_bf16(static_cast<float>(positions[t]));
-        const float f = round_bf16(pos * rope.inv_freq[tid]);
-        double s, c;
-        sincos(static_cast<double>(f), &s, &c);
-        const float cb = bf16_from_f64(c), sb = bf16_from_f64(s);
-        cs[tid] = make_uint2(pack_bf16(cb, sb), pack_bf16(sb, cb));  // exact: bf16 values
+    // ---- 2. cos/sin of the q/k rows' positions (table, or computed past its end)
+    if (do_rope) {
+#pragma unroll
+      for (int k = 0; k < kRowsPerHw; ++k) {
+        if (tok[k] < 0 || head[k] >= a.Hq + a.Hkv) continue;
+        if (pos[k] >= 0 && pos[k] < a.table_len) {
+          tab[k] = __ldg(a.rope_table + static_cast<int64_t>(pos[k]) * 16 + l16);
+        } else {
+          tab[k].x = rope_word(pos[k], a.rope.inv_freq[l16 * 4 + 0]);
+          tab[k].y = rope_word(pos[k], a.rope.inv_freq[l16 * 4 + 1]);
+          tab[k].z = rope_word(pos[k], a.rope.inv_freq[l16 * 4 + 2]);
+          tab[k].w = rope_word(pos[k], a.rope.inv_freq[l16 * 4 + 3]);
+        }
       }
-      __syncthreads();
     }
     // ---- 3. norm, rope, stores
 #pragma unroll
     for (int k = 0; k < kRowsPerHw; ++k) {
-      const int hidx = base + hw + 16 * k;
-      if (hidx >= heads) break;
-      const int kind = hidx < Hq ? 0 : hidx < Hq + Hkv ? 1 : 2;  // q, k, v
-      const int h = kind == 0 ? hidx : kind == 1 ? hidx - Hq : hidx - Hq - Hkv;
+      if (tok[k] < 0) continue;
+      const int h = head[k];
+      const int64_t t = a.t_begin + tok[k];
       uint32_t wd[4] = {raw[k].x, raw[k].y, raw[k].z, raw[k].w};
-      if (kind != 2) {
-        const __nv_bfloat16 *w = kind == 0 ? q_w : k_w;
-        if (do_norm) {
-          // flax RMSNorm: y = bf16(x * (rsqrt(mean(x^2) + eps) * scale)), fp32
-          double ss = 0.0;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const double lo = bf16_lo(wd[j]), hi = bf16_hi(wd[j]);
-            ss += lo * lo + hi * hi;
-          }
-          // the two half-warps of a warp may hold different kinds of rows
-          // (odd head counts under tensor parallelism): reduce within the half
-          const unsigned half_mask = 0xffffu << (16 * (hw & 1));
-#pragma unroll
-          for (int o = 8; o >= 1; o >>= 1) ss += __shfl_xor_sync(half_mask, ss, o);
-          // mean = sum / 128: a power-of-two scale, exact as a multiply
-          const float ms = __fmul_rn(static_cast<float>(ss), 1.0f / kHeadDim);
-          const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
-          const uint4 wr = __ldg(reinterpret_cast<const uint4 *>(w + l16 * 8));
-          const uint32_t ww[4] = {wr.x, wr.y, wr.z, wr.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float m0 = __fmul_rn(inv, bf16_lo(ww[j]));
-            const float m1 = __fmul_rn(inv, bf16_hi(ww[j]));
-            wd[j] = pack_bf16(__fmul_rn(bf16_lo(wd[j]), m0), __fmul_rn(bf16_hi(wd[j]), m1));
-          }
-        }
-        if (do_rope) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            // pair (x1, x2) = word j; stack((x1*cos - x2*sin, x1*sin + x2*cos), -1)
-            // with every op rounded to bf16: the products of bf16 values are
-            // exact before their rounding, so bf16x2 multiplies give the same
-            // bits; the sum and difference round through fp32 as before
-            const uint2 c = cs[l16 * 4 + j];
-            const uint32_t ab = bf16x2_mul(wd[j], c.x);   // (x1*cos, x2*sin)
-            const uint32_t de = bf16x2_mul(wd[j], c.y);   // (x1*sin, x2*cos)
-            wd[j] = pack_bf16(__fsub_rn(bf16_lo(ab), bf16_hi(ab)),
-                              __fadd_rn(bf16_lo(de), bf16_hi(de)));
-          }
-        }
-      }
-      const uint4 outv = make_uint4(wd[0], wd[1], wd[2], wd[3]);
-      if (kind == 0) {
-        *reinterpret_cast<uint4 *>(q_out + (t * Hq + h) * kHeadDim + l16 * 8) = outv;
+      if (h < a.Hq) {
+        norm_rope_slice(wd, qw, tab[k], half_mask, a.eps, do_norm, do_rope, qscale);
+        __stcs(reinterpret_cast<uint4 *>(a.q_out + (t * a.Hq + h) * kHeadDim + l16 * 8),
+               make_uint4(wd[0], wd[1], wd[2], wd[3]));
         continue;
       }
-      if (kind == 1 && k_out != nullptr) {
-        *reinterpret_cast<uint4 *>(k_out + (t * Hkv + h) * kHeadDim + l16 * 8) = outv;
+      const bool is_k = h < a.Hq + a.Hkv;
+      const int hk = is_k ? h - a.Hq : h - a.Hq - a.Hkv;
+      if (is_k) {
+        norm_rope_slice(wd, kw, tab[k], half_mask, a.eps, do_norm, do_rope, 0);
+        if (a.k_out != nullptr) {
+          *reinterpret_cast<uint4 *>(a.k_out + (t * a.Hkv + hk) * kHeadDim + l16 * 8) =
+              make_uint4(wd[0], wd[1], wd[2], wd[3]);
+        }
       }
-      if (slot < 0 || slot >= num_slots) continue;  // mode="drop"
-      const int64_t blk = slot / block_size, off = slot % block_size;
-      __nv_bfloat16 *dst = (kind == 1 ? k_cache : v_cache) + blk * sb + off * st + h * sh;
-      *reinterpret_cast<uint4 *>(dst + l16 * 8) = outv;
+      int64_t slot = __ldg(a.slots + t);
+      if (slot < 0 && (a.flags & VJ_KV_WRAP_NEGATIVE)) slot += a.num_slots;
+      if (slot < 0 || slot >= a.num_slots) continue;  // mode="drop"
+      const int64_t blk = a.bs_shift >= 0 ? slot >> a.bs_shift : slot / a.block_size;
+      const int64_t off = a.bs_shift >= 0 ? slot & (a.block_size - 1) : slot % a.block_size;
+      __nv_bfloat16 *dst = (is_k ? a.k_cache : a.v_cache) + blk * a.sb + off * a.st + hk * a.sh;
+      *reinterpret_cast<uint4 *>(dst + l16 * 8) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
     }
   }
 }
@@ -195,6 +321,32 @@ void build_rope_table(float rope_theta, float *inv_freq) {
 
 }  // namespace vj
 
+extern "C" size_t vj_rope_table_bytes(int32_t num_positions, int32_t head_dim) {
+  if (num_positions <= 0 || head_dim != vj::kHeadDim) return 0;
+  return static_cast<size_t>(num_positions) * (vj::kHeadDim / 2) * sizeof(uint32_t);
+}
+
+extern "C" vj_status vj_rope_table_build(void *table, int32_t num_positions, int32_t head_dim,
+                                         float rope_theta, cudaStream_t stream) {
+  using namespace vj;
+  if (head_dim != kHeadDim) {
+    return set_error(VJ_ERR_UNSUPPORTED, "vj_rope_table_build: head_dim must be 128, got " +
+                                             std::to_string(head_dim));
+  }
+  if (num_positions <= 0 || table == nullptr ||
+      reinterpret_cast<uintptr_t>(table) % 16 != 0) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT,
+                     "vj_rope_table_build: need a 16-byte aligned table and num_positions > 0");
+  }
+  RopeTable rope;
+  build_rope_table(rope_theta, rope.inv_freq);
+  const int64_t n = static_cast<int64_t>(num_positions) * kPairs;
+  const int grid = static_cast<int>(std::min<int64_t>((n + 255) / 256, 148 * 16));
+  rope_table_kernel<<<grid, 256, 0, stream>>>(static_cast<uint32_t *>(table), num_positions,
+                                               rope);
+  return check_launch("vj_rope_table_build");
+}
+
 extern "C" vj_status vj_kv_store_qknorm_rope(
     const void *q_in, const void *k_in, const void *v_in, const void *q_norm_w,
     const void *k_norm_w, const int32_t *positions, const int32_t *slot_mapping,
@@ -202,15 +354,24 @@ extern "C" vj_status vj_kv_store_qknorm_rope(
     int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
     int64_t num_blocks, int32_t block_size, int64_t stride_block,
     int64_t stride_token, int64_t stride_head, int64_t q_row_stride, int64_t k_row_stride,
-    int64_t v_row_stride, float eps, float rope_theta, int32_t flags, cudaStream_t stream) {
+    int64_t v_row_stride, const void *rope_table, int32_t rope_table_len, float eps,
+    float rope_theta, int32_t flags, cudaStream_t stream) {
   using namespace vj;
   if (num_tokens < 0 || num_q_heads < 0 || num_kv_heads <= 0 || num_blocks <= 0 ||
-      block_size <= 0) {
+      block_size <= 0 || rope_table_len < 0) {
     return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_kv_store_qknorm_rope: negative or zero size");
   }
   if (head_dim != kHeadDim) {
     return set_error(VJ_ERR_UNSUPPORTED, "vj_kv_store_qknorm_rope: head_dim must be 128, got " +
                                              std::to_string(head_dim));
+  }
+  const int heads = num_q_heads + 2 * num_kv_heads;
+  if (heads > 4096) {
+    return set_error(VJ_ERR_UNSUPPORTED, "vj_kv_store_qknorm_rope: more than 4096 head rows");
+  }
+  if ((flags & VJ_KV_QSCALE_DIV_SQRT_D) && (flags & VJ_KV_QSCALE_MUL_RSQRT_D)) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT,
+                     "vj_kv_store_qknorm_rope: choose one q scaling flag");
   }
   if (num_tokens == 0) return VJ_OK;
   if (!k_in || !v_in || !slot_mapping || !k_cache || !v_cache ||
@@ -223,30 +384,74 @@ extern "C" vj_status vj_kv_store_qknorm_rope(
   if ((flags & VJ_KV_ROPE) && !positions) {
     return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_kv_store_qknorm_rope: VJ_KV_ROPE needs positions");
   }
+  if (rope_table_len > 0 && (rope_table == nullptr ||
+                             reinterpret_cast<uintptr_t>(rope_table) % 16 != 0)) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT,
+                     "vj_kv_store_qknorm_rope: rope_table must be 16-byte aligned");
+  }
   if (q_row_stride == 0) q_row_stride = (int64_t)num_q_heads * kHeadDim;
   if (k_row_stride == 0) k_row_stride = (int64_t)num_kv_heads * kHeadDim;
   if (v_row_stride == 0) v_row_stride = (int64_t)num_kv_heads * kHeadDim;
   if ((q_row_stride | k_row_stride | v_row_stride) % 8 != 0 ||
       (reinterpret_cast<uintptr_t>(q_in) | reinterpret_cast<uintptr_t>(k_in) |
-       reinterpret_cast<uintptr_t>(v_in)) % 16 != 0) {
+       reinterpret_cast<uintptr_t>(v_in) | reinterpret_cast<uintptr_t>(q_out) |
+       reinterpret_cast<uintptr_t>(k_out)) % 16 != 0 ||
+      ((flags & VJ_KV_NORM) && (reinterpret_cast<uintptr_t>(q_norm_w) |
+                                reinterpret_cast<uintptr_t>(k_norm_w)) % 16 != 0)) {
     return set_error(VJ_ERR_INVALID_ARGUMENT,
-                     "vj_kv_store_qknorm_rope: q/k/v rows must start on 16-byte boundaries");
+                     "vj_kv_store_qknorm_rope: q/k/v rows and weights must start on 16-byte "
+                     "boundaries");
   }
   if ((stride_block | stride_token | stride_head) % 8 != 0 ||
       (reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) % 16 != 0) {
     return set_error(VJ_ERR_INVALID_ARGUMENT,
                      "vj_kv_store_qknorm_rope: cache base/strides must be 16-byte aligned");
   }
-  RopeTable rope;
-  build_rope_table(rope_theta, rope.inv_freq);
-  const int64_t grid = num_tokens;
-  kv_store_qknorm_rope_kernel<<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(
-      static_cast<const __nv_bfloat16 *>(q_in), static_cast<const __nv_bfloat16 *>(k_in),
-      static_cast<const __nv_bfloat16 *>(v_in), static_cast<const __nv_bfloat16 *>(q_norm_w),
-      static_cast<const __nv_bfloat16 *>(k_norm_w), positions, slot_mapping,
-      static_cast<__nv_bfloat16 *>(q_out), static_cast<__nv_bfloat16 *>(k_out),
-      static_cast<__nv_bfloat16 *>(k_cache), static_cast<__nv_bfloat16 *>(v_cache), num_tokens,
-      num_q_heads, num_kv_heads, num_blocks * block_size, block_size, stride_block, stride_token,
-      stride_head, q_row_stride, k_row_stride, v_row_stride, eps, flags, rope);
-  return check_launch("vj_kv_store_qknorm_rope");
+  KvArgs a;
+  a.q_in = static_cast<const __nv_bfloat16 *>(q_in);
+  a.k_in = static_cast<const __nv_bfloat16 *>(k_in);
+  a.v_in = static_cast<const __nv_bfloat16 *>(v_in);
+  a.q_w = static_cast<const __nv_bfloat16 *>(q_norm_w);
+  a.k_w = static_cast<const __nv_bfloat16 *>(k_norm_w);
+  a.positions = positions;
+  a.slots = slot_mapping;
+  a.q_out = static_cast<__nv_bfloat16 *>(q_out);
+  a.k_out = static_cast<__nv_bfloat16 *>(k_out);
+  a.k_cache = static_cast<__nv_bfloat16 *>(k_cache);
+  a.v_cache = static_cast<__nv_bfloat16 *>(v_cache);
+  a.rope_table = static_cast<const uint4 *>(rope_table);
+  a.table_len = rope_table_len > 0 ? rope_table_len : 0;
+  a.Hq = num_q_heads;
+  a.Hkv = num_kv_heads;
+  a.heads = heads;
+  a.heads_magic = static_cast<uint32_t>((1ull << 32) / static_cast<uint64_t>(heads) + 1);
+  a.num_slots = num_blocks * block_size;
+  a.block_size = block_size;
+  a.bs_shift = (block_size & (block_size - 1)) == 0 ? __builtin_ctz(block_size) : -1;
+  a.sb = stride_block;
+  a.st = stride_token;
+  a.sh = stride_head;
+  a.qrs = q_row_stride;
+  a.krs = k_row_stride;
+  a.vrs = v_row_stride;
+  a.eps = eps;
+  a.flags = flags;
+  build_rope_table(rope_theta, a.rope.inv_freq);
+  // __umulhi(r, magic) == r / heads exactly while r * heads < 2^32 (the
+  // magic's excess over 2^32 / heads is below 1): launch in token ranges
+  // that keep every row index within that bound
+  const int64_t max_rows = static_cast<int64_t>((1ull << 32) / static_cast<uint64_t>(heads)) - 1;
+  const int64_t tokens_per_launch = std::max<int64_t>(1, max_rows / heads);
+  const int64_t grid_cap = static_cast<int64_t>(num_sms()) * 8;
+  for (int64_t t0 = 0; t0 < num_tokens; t0 += tokens_per_launch) {
+    const int64_t nt = std::min(tokens_per_launch, num_tokens - t0);
+    a.t_begin = t0;
+    a.num_rows = static_cast<uint32_t>(nt * heads);
+    const int64_t chunks = (static_cast<int64_t>(a.num_rows) + kRowsPerCta - 1) / kRowsPerCta;
+    const unsigned grid = static_cast<unsigned>(std::min(chunks, grid_cap));
+    kv_store_rows_kernel<<<grid, kThreads, 0, stream>>>(a);
+    const vj_status st = check_launch("vj_kv_store_qknorm_rope");
+    if (st != VJ_OK) return st;
+  }
+  return VJ_OK;
 }

@@ -27,7 +27,10 @@ PROTOTYPES: dict[str, tuple] = {
         c_i64, c_i32, c_i32, c_i32, c_i64, c_i32,   # T, Hq, Hkv, D, nb, bs
         c_i64, c_i64, c_i64,                        # strides (block, token, head)
         c_i64, c_i64, c_i64,                        # q/k/v row strides (0 = packed)
+        c_vp, c_i32,                                # rope_table, rope_table_len
         c_f32, c_f32, c_i32, c_vp]),                # eps, theta, flags, stream
+    "vj_rope_table_bytes": (c_sz, [c_i32, c_i32]),
+    "vj_rope_table_build": (c_int, [c_vp, c_i32, c_i32, c_f32, c_vp]),
     "vj_paged_decode_workspace_size": (c_sz, [c_i32, c_i32, c_i32, c_i32]),
     "vj_paged_decode": (c_int, [
         c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,         # q, k_cache, v_cache, bt, lens, out
@@ -35,7 +38,6 @@ PROTOTYPES: dict[str, tuple] = {
         c_i32, c_i32,                               # bt_width, bt_stride
         c_i64, c_i64, c_i64,                        # strides
         c_f32, c_i32, c_vp, c_sz, c_vp]),           # scale, max_chunks, ws, ws_bytes, stream
-    "vj_paged_decode_noalloc_scratch_bytes": (c_sz, []),
     "vj_paged_decode_planned": (c_int, [
         c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,         # q, k_cache, v_cache, bt, lens, out
         c_i32, c_i32, c_i32, c_i32, c_i64, c_i32,   # B, Hq, Hkv, D, nb, bs
@@ -82,6 +84,7 @@ PROTOTYPES: dict[str, tuple] = {
 # vj_status codes (include/vjattn.h)
 VJ_OK, VJ_ERR_INVALID_ARGUMENT, VJ_ERR_UNSUPPORTED, VJ_ERR_WORKSPACE, VJ_ERR_CUDA = range(5)
 VJ_KV_NORM, VJ_KV_ROPE, VJ_KV_WRAP_NEGATIVE = 1, 2, 4
+VJ_KV_QSCALE_DIV_SQRT_D, VJ_KV_QSCALE_MUL_RSQRT_D = 8, 16
 VJ_META_PREFILL, VJ_META_DECODE, VJ_META_RANGES = 0, 1, 2
 VJ_META_LAST_BLOCK_SLOT = 1
 

@@ -27,6 +27,36 @@ def _cache_views(kv_cache: torch.Tensor):
     return k, v, nb, bs, (k.stride(0), k.stride(1), k.stride(2))
 
 
+_rope_tables: dict[tuple[int, float], torch.Tensor] = {}
+_retired_tables: list[torch.Tensor] = []
+DEFAULT_ROPE_POSITIONS = 4096
+
+
+def rope_table(device: torch.device, rope_theta: float = 1e6,
+               num_positions: int = DEFAULT_ROPE_POSITIONS) -> torch.Tensor:
+    """The (cos, sin) bf16 pair table of positions [0, num_positions) for
+    rope_theta on `device` (vj_rope_table_build), cached per device and theta
+    and only grown. An outgrown table is retired, not freed, because a CUDA
+    graph captured with it keeps reading its address. Positions past the end
+    of the table are computed inside the kernel (same bits, slower)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx, float(rope_theta))
+    t = _rope_tables.get(key)
+    if t is None or t.numel() < num_positions * 64:
+        if t is not None:
+            _retired_tables.append(t)
+        n = max(num_positions, DEFAULT_ROPE_POSITIONS)
+        nbytes = _native.load().vj_rope_table_bytes(n, 128)
+        t = torch.empty(nbytes // 4, dtype=torch.int32, device=device)
+        _native.call("vj_rope_table_build", t.data_ptr(), n, 128, float(rope_theta),
+                     stream_ptr(device))
+        _rope_tables[key] = t
+    return t
+
+
+_QSCALE = {None: 0, "div": 8, "mul": 16}
+
+
 def kv_store_qknorm_rope(q: torch.Tensor | None, k: torch.Tensor, v: torch.Tensor,
                          kv_cache: torch.Tensor, slot_mapping: torch.Tensor,
                          positions: torch.Tensor | None = None,
@@ -36,11 +66,17 @@ def kv_store_qknorm_rope(q: torch.Tensor | None, k: torch.Tensor, v: torch.Tenso
                          norm: bool = True, rope: bool = True,
                          wrap_negative_slots: bool = True,
                          q_out: torch.Tensor | None = None,
-                         return_k: bool = False):
-    """One launch: q_out = rope(norm(q)), cache[slot] = (rope(norm(k)), v).
+                         return_k: bool = False,
+                         q_scale: str | None = None,
+                         table: torch.Tensor | None = None):
+    """One launch: q_out = scale(rope(norm(q))), cache[slot] = (rope(norm(k)), v).
 
     q [T, Hq, D] (or None), k/v [T, Hkv, D] bf16; slot_mapping/positions [T]
-    int32. Returns q_out (and k_out if return_k)."""
+    int32. q_scale: None, "div" (bf16(q / bf16(sqrt(D))), the reference's
+    decode scaling, vllm/model/qwen3.py:207) or "mul" (bf16(q *
+    bf16(1/sqrt(D))), its prefill kernel's, prefill_paged_attention.py:60).
+    table: a rope_table() for rope_theta (default: the cached one of this
+    device). Returns q_out (and k_out if return_k)."""
     dev = require_cuda(k, v, kv_cache, slot_mapping)
     kc, vc, nb, bs, (sb, st, sh) = _cache_views(kv_cache)
     T, Hkv, D = k.shape
@@ -76,14 +112,20 @@ def kv_store_qknorm_rope(q: torch.Tensor | None, k: torch.Tensor, v: torch.Tenso
         require_dtype(positions, torch.int32, "positions")
     if wrap_negative_slots:
         flags |= _native.VJ_KV_WRAP_NEGATIVE
+    if q_scale not in _QSCALE:
+        raise ValueError(f"q_scale must be None, 'div' or 'mul'; got {q_scale!r}")
+    flags |= _QSCALE[q_scale]
+    if rope and table is None:
+        table = rope_table(dev, rope_theta)
+    tab_len = table.numel() // 64 if (rope and table is not None) else 0
     k_out = torch.empty((T, Hkv, D), dtype=k.dtype, device=k.device) if return_k else None
     _native.call("vj_kv_store_qknorm_rope",
                  ptr(q), k.data_ptr(), v.data_ptr(), ptr(q_norm_weight if norm else None),
                  ptr(k_norm_weight if norm else None), ptr(positions if rope else None),
                  slot_mapping.data_ptr(), ptr(q_out), ptr(k_out), kc.data_ptr(), vc.data_ptr(),
                  T, Hq, Hkv, D, nb, bs, sb, st, sh, q.stride(0) if q is not None else 0,
-                 k.stride(0), v.stride(0), float(eps), float(rope_theta), flags,
-                 stream_ptr(dev))
+                 k.stride(0), v.stride(0), ptr(table) if tab_len else None, tab_len,
+                 float(eps), float(rope_theta), flags, stream_ptr(dev))
     if return_k:
         return q_out, k_out
     return q_out

@@ -28,7 +28,7 @@ import torch.nn.functional as F
 
 from ..kernels.decode_paged_attention import paged_decode
 from ..kernels.fused import add_rmsnorm, silu_mul
-from ..kernels.kv_store import kv_store_qknorm_rope, update_kv_cache
+from ..kernels.kv_store import kv_store_qknorm_rope
 from ..kernels.prefill_paged_attention import paged_prefill
 
 
@@ -90,14 +90,22 @@ class PrefillAttentionMetadata:
 def attention(kv_cache: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
               metadata) -> tuple[torch.Tensor, torch.Tensor]:
     """Drop-in for vllm/model/qwen3.py:172-218: store k/v (in place), then paged
-    prefill or decode attention. Returns (kv_cache, out [T, Hq, D])."""
-    update_kv_cache(kv_cache, metadata.slot_mapping, k, v)
-    if isinstance(metadata, PrefillAttentionMetadata):
+    prefill or decode attention. Returns (kv_cache, out [T, Hq, D]).
+
+    q is scaled the reference's way, in bf16, by the same launch that stores
+    k/v: decode divides by bf16(sqrt(D)) (qwen3.py:207), prefill multiplies
+    by bf16(1/sqrt(D)) (prefill_paged_attention.py:60); attention then runs
+    with scale 1."""
+    prefill = isinstance(metadata, PrefillAttentionMetadata)
+    qs = kv_store_qknorm_rope(q, k, v, kv_cache, metadata.slot_mapping, norm=False, rope=False,
+                              q_scale="mul" if prefill else "div")
+    if prefill:
         S = metadata.num_seqs if metadata.num_seqs is not None else metadata.block_tables.shape[0]
-        out = paged_prefill(q, kv_cache, metadata.block_tables[:S], metadata.cu_seqlens_q[:S + 1],
-                            metadata.context_lens, max_seqlen_q=metadata.max_seqlen_bucket)
+        out = paged_prefill(qs, kv_cache, metadata.block_tables[:S],
+                            metadata.cu_seqlens_q[:S + 1], metadata.context_lens,
+                            max_seqlen_q=metadata.max_seqlen_bucket, scale=1.0)
     else:
-        out = paged_decode(q, kv_cache, metadata.block_tables, metadata.context_lens)
+        out = paged_decode(qs, kv_cache, metadata.block_tables, metadata.context_lens, 1.0)
     return kv_cache, out
 
 
@@ -189,7 +197,8 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
 class Qwen3Model:
     """Forward passes of one rank. kv_caches[l]: (2, num_blocks, bs, Hkv_l, D) bf16."""
 
-    def __init__(self, weights: Qwen3Weights, process_group=None, tp_comm=None):
+    def __init__(self, weights: Qwen3Weights, process_group=None, tp_comm=None,
+                 reference_q_scaling: bool = False):
         self.w = weights
         self.cfg = weights.cfg
         self.pg = process_group
@@ -201,6 +210,14 @@ class Qwen3Model:
         self.hkv = c.num_key_value_heads // weights.tp_size
         self.d = c.head_dim
         self.scale = 1.0 / math.sqrt(c.head_dim)
+        # reference_q_scaling: K3 scales q in bf16 like the reference (decode:
+        # q / bf16(sqrt(D)), qwen3.py:207; prefill: q * bf16(1/sqrt(D)),
+        # prefill_paged_attention.py:60) and attention runs with scale 1;
+        # otherwise the attention kernels apply 1/sqrt(D) to q.k in fp32
+        self.reference_q_scaling = reference_q_scaling
+        # (cos, sin) table of K3 covering every position the engine can reach;
+        # set by the model runner before any CUDA graph capture
+        self.rope_table: torch.Tensor | None = None
         # split-KV scratch of the decode kernel, owned here so that captured
         # CUDA graphs keep a valid address (set by the model runner)
         self.decode_workspace: torch.Tensor | None = None
@@ -226,7 +243,7 @@ class Qwen3Model:
         return add_rmsnorm(d, w_norm, eps, residual=x)
 
     def _layer(self, l: int, x: torch.Tensor, h: torch.Tensor, kv_cache: torch.Tensor, meta,
-               attn_fn, w_next: torch.Tensor):
+               attn_fn, w_next: torch.Tensor, q_scale: str | None):
         """x: residual stream entering layer l; h = input_layernorm(x). Returns
         (x after the layer, h = the next norm of it, with weight w_next)."""
         lw = self.w.layers[l]
@@ -237,7 +254,8 @@ class Qwen3Model:
         q = kv_store_qknorm_rope(q.view(T, self.hq, self.d), k.view(T, self.hkv, self.d),
                                  v.view(T, self.hkv, self.d), kv_cache,
                                  meta.slot_mapping, meta.positions, lw.q_norm, lw.k_norm,
-                                 eps=c.rms_norm_eps, rope_theta=c.rope_theta)
+                                 eps=c.rms_norm_eps, rope_theta=c.rope_theta,
+                                 q_scale=q_scale, table=self.rope_table)
         o = attn_fn(q, kv_cache).reshape(T, self.hq * self.d)
         # attn_output += x; post_attention_layernorm   (qwen3.py:375-389)
         x, h = self._reduce_add_norm(o, lw.w_o, x, lw.ln2, 0)
@@ -245,14 +263,21 @@ class Qwen3Model:
         # outputs = residual + mlp; next input_layernorm (or the final norm)
         return self._reduce_add_norm(m, lw.w_down, x, w_next, 1)
 
-    def _stack(self, x: torch.Tensor, kv_caches, meta, attn_fn) -> torch.Tensor:
+    def _stack(self, x: torch.Tensor, kv_caches, meta, attn_fn,
+               q_scale: str | None = None) -> torch.Tensor:
         c = self.cfg
         L = c.num_hidden_layers
         h = add_rmsnorm(x, self.w.layers[0].ln1, c.rms_norm_eps)
         for l in range(L):
             w_next = self.w.layers[l + 1].ln1 if l + 1 < L else self.w.norm
-            x, h = self._layer(l, x, h, kv_caches[l], meta, attn_fn, w_next)
+            x, h = self._layer(l, x, h, kv_caches[l], meta, attn_fn, w_next, q_scale)
         return h    # final norm applied
+
+    def _attn_scale(self, kind: str) -> tuple[str | None, float]:
+        """(K3 q scaling, attention scale) of a prefill or decode forward."""
+        if self.reference_q_scaling:
+            return ("mul" if kind == "prefill" else "div"), 1.0
+        return None, self.scale
 
     def embed(self, input_ids: torch.Tensor) -> torch.Tensor:
         return F.embedding(input_ids.long(), self.w.embed)
@@ -263,27 +288,29 @@ class Qwen3Model:
         no logits in prefill, model_runner.py:41-59)."""
         x = self.embed(meta.input_ids)
         S = meta.num_seqs
+        q_scale, scale = self._attn_scale("prefill")
 
         def attn(q, kv):
             return paged_prefill(q, kv, meta.block_tables[:S], meta.cu_seqlens_q[:S + 1],
                                  getattr(meta, "context_lens", None),
-                                 max_seqlen_q=meta.max_seqlen_bucket, scale=self.scale)
+                                 max_seqlen_q=meta.max_seqlen_bucket, scale=scale)
 
-        return self._stack(x, kv_caches, meta, attn)
+        return self._stack(x, kv_caches, meta, attn, q_scale)
 
     def forward_decode(self, meta, kv_caches: list[torch.Tensor]) -> torch.Tensor:
         """One token per row; returns bf16 logits [rows, vocab]."""
         x = self.embed(meta.input_ids)
         planned = []   # the first layer plans the split; the others reuse it
+        q_scale, scale = self._attn_scale("decode")
 
         def attn(q, kv):
-            out = paged_decode(q, kv, meta.block_tables, meta.context_lens, self.scale,
+            out = paged_decode(q, kv, meta.block_tables, meta.context_lens, scale,
                                workspace=self.decode_workspace,
                                reuse_plan=bool(planned) and self.decode_workspace is not None)
             planned.append(True)
             return out
 
-        x = self._stack(x, kv_caches, meta, attn)
+        x = self._stack(x, kv_caches, meta, attn, q_scale)
         return F.linear(x, self.w.lm_head)           # compute_logits (qwen3.py:474-477)
 
     def forward_mixed(self, meta, kv_caches: list[torch.Tensor], num_decode: int,

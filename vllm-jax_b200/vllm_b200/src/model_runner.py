@@ -20,6 +20,7 @@ import torch
 from .. import _native
 from ..config import Config
 from ..kernels.decode_paged_attention import decode_workspace_bytes
+from ..kernels.kv_store import rope_table
 from ..kernels.metadata import DecodeMeta, DeviceTables, bucket_size
 from ..kernels.sampler import sample
 from ..model.qwen3 import Qwen3Config, Qwen3Model, Qwen3Weights
@@ -74,7 +75,12 @@ class ModelRunner:
         self.block_size = config.block_size
         self.width = config.max_blocks_per_seq
         self.weights = weights or Qwen3Weights(model_cfg, device, seed, tp_rank, tp_size)
-        self.model = Qwen3Model(self.weights, process_group, tp_comm)
+        # compat=True also follows the reference's bf16 q scaling
+        self.model = Qwen3Model(self.weights, process_group, tp_comm,
+                                reference_q_scaling=config.compat)
+        # RoPE (cos, sin) table of every position a request can reach, built
+        # before any graph capture (positions repeat across layers and steps)
+        self.model.rope_table = rope_table(device, model_cfg.rope_theta, config.max_len + 1)
         # one decode workspace for the largest batch bucket, allocated before
         # any graph capture and never replaced
         self.model.decode_workspace = torch.empty(
@@ -99,6 +105,9 @@ class ModelRunner:
         self.graphs: dict[int, tuple[torch.cuda.CUDAGraph, DecodeMeta, torch.Tensor]] = {}
         self.graph_launches: dict[int, int] = {}
         n = max(config.max_num_seqs, 1)
+        # when a list: (start, end) CUDA events of every decode forward, for
+        # measuring decode-step device time (bench.py's roofline)
+        self.decode_events: list | None = None
         self._tok_ring = [torch.empty(n, dtype=torch.int32).pin_memory() for _ in range(4)]
         self._tok_events: list[torch.cuda.Event | None] = [None] * 4
         self._tok_next = 0
@@ -200,6 +209,10 @@ class ModelRunner:
         B = len(requests)
         bb = bucket_size(B)
         words = sampling_words(requests)
+        ev = None
+        if self.decode_events is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record(torch.cuda.current_stream(self.device))
         if self.use_cuda_graphs:
             graph, meta, logits = self._decode_graph(bb)
             self.tables.build_decode(slots, lens, self.width, out=meta,
@@ -210,6 +223,9 @@ class ModelRunner:
             meta = self.tables.build_decode(slots, lens, self.width,
                                             last_block_slot=self.config.compat, extra=words)
             logits = self.model.forward_decode(meta, self.kv_caches)
+        if ev is not None:
+            ev[1].record(torch.cuda.current_stream(self.device))
+            self.decode_events.append(ev)
         d_slots, d_lens = self.tables.last_lists()
         toks = self._draw(logits[:B], d_slots, d_lens, self.tables.last_extra())
         return self._tokens_to_host(toks)
