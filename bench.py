@@ -507,7 +507,7 @@ def run_kvstore(args, rank, world, local_rank):
                    "l2": f"inputs larger than L2 ({step_bytes / 1e9:.2f} GB per step)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                     "peak_source": f"{peak_src} hbm_gbs", "kernel": "kv_store_rows_kernel",
+                     "peak_source": f"{peak_src} hbm_gbs", "kernel": "kv_store_tma_kernel",
                      "traffic": (int(KVSTORE_PROFILE["dram_bytes"] * T / KVSTORE_PROFILE["tokens"])
                                  if world == 1 else None),
                      "traffic_source": "ncu dram bytes of a 16-sequence C2 capture, scaled by "

@@ -111,6 +111,12 @@ VJ_API vj_status vj_kv_store_qknorm_rope(
     const void *rope_table, int32_t rope_table_len,
     float eps, float rope_theta, int32_t flags, cudaStream_t stream);
 
+/* Number of bounded waits of vj_kv_store_qknorm_rope's staged kernel that
+ * ran out (2 s each) since the library was loaded or last reset; nonzero means
+ * a call's output is incomplete. Synchronous (reads a device word). No
+ * counterpart in the reference. */
+VJ_API vj_status vj_kv_store_timeouts(int32_t *count, int32_t reset);
+
 /* RoPE table for vj_kv_store_qknorm_rope: for each position p < num_positions
  * and pair i < D/2, the bf16 word pair (cos, sin) of bf16(bf16(p) *
  * inv_freq[i]) (vllm/model/qwen3.py:62-67), inv_freq in bf16 from the bf16

@@ -153,3 +153,14 @@ def test_kv_store_rejects_bad_args():
         kv_store_qknorm_rope(None, k, k, cache, slots, norm=False, rope=False)
     with pytest.raises(ValueError):
         kv_store_qknorm_rope(None, k, k, cache, slots.long(), norm=False, rope=False)
+
+
+def test_kv_store_no_wait_timed_out():
+    """Every call above completed without a staged-kernel wait running out."""
+    import ctypes
+
+    from vllm_b200 import _native
+    torch.cuda.synchronize()
+    n = ctypes.c_int32(-1)
+    _native.check(_native.load().vj_kv_store_timeouts(ctypes.byref(n), 0))
+    assert n.value == 0

@@ -305,6 +305,186 @@ kv_store_rows_kernel(const KvArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// TMA-staged variant: a persistent CTA streams "units" of G whole tokens
+// (G * heads rows, ~96 rows = 24 KB) through a kStages-deep shared-memory
+// ring. One producer thread loads a unit's positions and slots, then issues
+// untiled bulk copies (cp.async.bulk, no multicast) of its q, k and v rows and
+// of its tokens' (cos, sin) table rows, counted on the stage's full barrier;
+// 8 consumer warps (16 half-warps, one row each at a time) normalise, rotate,
+// scale and store, then release the stage. Loads of later units are in flight
+// while a unit is computed, so HBM stays busy with few registers per thread.
+// Every wait is bounded (2 s); a timed-out wait counts in g_kv_store_timeouts
+// and the CTA drains its copies in flight and returns.
+// ---------------------------------------------------------------------------
+constexpr int kStages = 4;
+constexpr int kConsumerWarps = 8;
+constexpr int kTmaThreads = 32 * (kConsumerWarps + 1);
+constexpr int kUnitRows = 96;
+constexpr int kMaxUnitTokens = 32;
+
+__device__ int g_kv_store_timeouts;
+
+struct TmaPlan {
+  int G;                 // tokens per unit
+  uint32_t rows_off, tab_off, meta_off, stage_bytes;
+  int64_t num_units;
+};
+
+__global__ void __launch_bounds__(kTmaThreads, 1)
+kv_store_tma_kernel(const KvArgs a, const TmaPlan p, int64_t num_tokens) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * p.stage_bytes);
+  uint64_t *empty = full + kStages;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const bool do_norm = (a.flags & VJ_KV_NORM) != 0;
+  const bool do_rope = (a.flags & VJ_KV_ROPE) != 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    if (lane != 0) return;
+    int64_t it = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < p.num_units; u += gridDim.x, ++it) {
+      const int stage = static_cast<int>(it % kStages);
+      if (it >= kStages && !mbar_wait(&empty[stage], static_cast<uint32_t>((it / kStages - 1) & 1))) {
+        atomicAdd(&g_kv_store_timeouts, 1);
+        ok = false;
+        break;
+      }
+      uint8_t *base = smem + stage * p.stage_bytes;
+      int2 *meta = reinterpret_cast<int2 *>(base + p.meta_off);
+      const int64_t t0 = u * p.G;
+      const int ng = static_cast<int>(num_tokens - t0 < p.G ? num_tokens - t0 : p.G);
+      uint32_t bytes = static_cast<uint32_t>(ng) * a.heads * 256u;
+#pragma unroll 4
+      for (int g = 0; g < ng; ++g) {
+        const int pos = do_rope ? __ldg(a.positions + t0 + g) : 0;
+        meta[g] = make_int2(pos, __ldg(a.slots + t0 + g));
+        if (do_rope && pos >= 0 && pos < a.table_len) bytes += 256u;
+      }
+      mbar_arrive_expect_tx(&full[stage], bytes);
+      for (int g = 0; g < ng; ++g) {
+        const int64_t t = t0 + g;
+        const int pos = meta[g].x;
+        uint8_t *rows = base + p.rows_off + static_cast<uint32_t>(g) * a.heads * 256u;
+        if (a.Hq > 0) bulk_g2s(rows, a.q_in + t * a.qrs, a.Hq * 256u, &full[stage]);
+        bulk_g2s(rows + a.Hq * 256u, a.k_in + t * a.krs, a.Hkv * 256u, &full[stage]);
+        bulk_g2s(rows + (a.Hq + a.Hkv) * 256u, a.v_in + t * a.vrs, a.Hkv * 256u, &full[stage]);
+        if (do_rope && pos >= 0 && pos < a.table_len) {
+          bulk_g2s(base + p.tab_off + g * 256u, a.rope_table + static_cast<int64_t>(pos) * 16,
+                   256u, &full[stage]);
+        }
+      }
+    }
+    // copies still in flight must land before the CTA exits (normal path: the
+    // consumers already waited for all of them)
+    if (!ok) {
+      for (int64_t j = it > kStages ? it - kStages : 0; j < it; ++j) {
+        mbar_wait(&full[j % kStages], static_cast<uint32_t>((j / kStages) & 1));
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int hw = threadIdx.x >> 4;   // 0..15
+  const int l16 = threadIdx.x & 15;
+  const unsigned half_mask = 0xffffu << (16 * (hw & 1));
+  const int qscale = a.flags & (VJ_KV_QSCALE_DIV_SQRT_D | VJ_KV_QSCALE_MUL_RSQRT_D);
+  uint32_t qw[4] = {0u, 0u, 0u, 0u}, kw[4] = {0u, 0u, 0u, 0u};
+  if (do_norm) {
+    if (a.Hq > 0) {
+      const uint4 t = __ldg(reinterpret_cast<const uint4 *>(a.q_w + l16 * 8));
+      qw[0] = t.x; qw[1] = t.y; qw[2] = t.z; qw[3] = t.w;
+    }
+    const uint4 t = __ldg(reinterpret_cast<const uint4 *>(a.k_w + l16 * 8));
+    kw[0] = t.x; kw[1] = t.y; kw[2] = t.z; kw[3] = t.w;
+  }
+  int64_t it = 0;
+  for (int64_t u = blockIdx.x; u < p.num_units; u += gridDim.x, ++it) {
+    const int stage = static_cast<int>(it % kStages);
+    if (!mbar_wait(&full[stage], static_cast<uint32_t>((it / kStages) & 1))) {
+      if (lane == 0) atomicAdd(&g_kv_store_timeouts, 1);
+      return;   // without arriving: the producer's wait runs out and it drains
+    }
+    const uint8_t *base = smem + stage * p.stage_bytes;
+    const int2 *meta = reinterpret_cast<const int2 *>(base + p.meta_off);
+    const int64_t t0 = u * p.G;
+    const int ng = static_cast<int>(num_tokens - t0 < p.G ? num_tokens - t0 : p.G);
+    const uint32_t nrows = static_cast<uint32_t>(ng) * a.heads;
+    for (uint32_t r = hw; r < nrows; r += 16) {
+      const int g = static_cast<int>(__umulhi(r, a.heads_magic));   // r / heads
+      const int h = static_cast<int>(r - static_cast<uint32_t>(g) * a.heads);
+      const int64_t t = t0 + g;
+      const uint4 raw = *reinterpret_cast<const uint4 *>(base + p.rows_off + r * 256u + l16 * 16u);
+      uint32_t wd[4] = {raw.x, raw.y, raw.z, raw.w};
+      const bool is_q = h < a.Hq, is_k = !is_q && h < a.Hq + a.Hkv;
+      if (is_q || is_k) {
+        uint4 tab = make_uint4(0u, 0u, 0u, 0u);
+        if (do_rope) {
+          const int pos = meta[g].x;
+          if (pos >= 0 && pos < a.table_len) {
+            tab = *reinterpret_cast<const uint4 *>(base + p.tab_off + g * 256u + l16 * 16u);
+          } else {
+            tab.x = rope_word(pos, a.rope.inv_freq[l16 * 4 + 0]);
+            tab.y = rope_word(pos, a.rope.inv_freq[l16 * 4 + 1]);
+            tab.z = rope_word(pos, a.rope.inv_freq[l16 * 4 + 2]);
+            tab.w = rope_word(pos, a.rope.inv_freq[l16 * 4 + 3]);
+          }
+        }
+        norm_rope_slice(wd, is_q ? qw : kw, tab, half_mask, a.eps, do_norm, do_rope,
+                        is_q ? qscale : 0);
+      }
+      if (is_q) {
+        __stcs(reinterpret_cast<uint4 *>(a.q_out + (t * a.Hq + h) * kHeadDim + l16 * 8),
+               make_uint4(wd[0], wd[1], wd[2], wd[3]));
+        continue;
+      }
+      const int hk = is_k ? h - a.Hq : h - a.Hq - a.Hkv;
+      if (is_k && a.k_out != nullptr) {
+        *reinterpret_cast<uint4 *>(a.k_out + (t * a.Hkv + hk) * kHeadDim + l16 * 8) =
+            make_uint4(wd[0], wd[1], wd[2], wd[3]);
+      }
+      int64_t slot = meta[g].y;
+      if (slot < 0 && (a.flags & VJ_KV_WRAP_NEGATIVE)) slot += a.num_slots;
+      if (slot < 0 || slot >= a.num_slots) continue;  // mode="drop"
+      const int64_t blk = a.bs_shift >= 0 ? slot >> a.bs_shift : slot / a.block_size;
+      const int64_t off = a.bs_shift >= 0 ? slot & (a.block_size - 1) : slot % a.block_size;
+      __nv_bfloat16 *dst = (is_k ? a.k_cache : a.v_cache) + blk * a.sb + off * a.st + hk * a.sh;
+      *reinterpret_cast<uint4 *>(dst + l16 * 8) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+  }
+}
+
+// Unit size and shared-memory layout of the staged kernel for `heads` rows
+// per token; stage_bytes == 0 when kStages stages of one token do not fit.
+TmaPlan plan_tma(int heads, int64_t num_tokens) {
+  TmaPlan p{};
+  p.G = std::max(1, std::min(kMaxUnitTokens, kUnitRows / heads));
+  const uint32_t rows = static_cast<uint32_t>(p.G) * heads * 256u;
+  p.rows_off = 0;
+  p.tab_off = rows;
+  p.meta_off = p.tab_off + p.G * 256u;
+  p.stage_bytes = (p.meta_off + p.G * 8u + 127u) & ~127u;
+  if (static_cast<size_t>(kStages) * p.stage_bytes + 2 * kStages * 8 > 200 * 1024) {
+    p.stage_bytes = 0;
+  }
+  p.num_units = (num_tokens + p.G - 1) / p.G;
+  return p;
+}
+
 }  // namespace
 
 // inv_freq = 1 / rope_theta ** (arange(0, D, 2, bf16) / D), all in bf16
@@ -320,6 +500,25 @@ void build_rope_table(float rope_theta, float *inv_freq) {
 }
 
 }  // namespace vj
+
+extern "C" vj_status vj_kv_store_timeouts(int32_t *count, int32_t reset) {
+  using namespace vj;
+  if (count == nullptr) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_kv_store_timeouts: null count");
+  }
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_kv_store_timeouts, sizeof(int)) != cudaSuccess) {
+    return set_error(VJ_ERR_CUDA, "vj_kv_store_timeouts: cudaMemcpyFromSymbol failed");
+  }
+  *count = v;
+  if (reset) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_kv_store_timeouts, &zero, sizeof(int)) != cudaSuccess) {
+      return set_error(VJ_ERR_CUDA, "vj_kv_store_timeouts: cudaMemcpyToSymbol failed");
+    }
+  }
+  return VJ_OK;
+}
 
 extern "C" size_t vj_rope_table_bytes(int32_t num_positions, int32_t head_dim) {
   if (num_positions <= 0 || head_dim != vj::kHeadDim) return 0;
@@ -437,6 +636,32 @@ extern "C" vj_status vj_kv_store_qknorm_rope(
   a.eps = eps;
   a.flags = flags;
   build_rope_table(rope_theta, a.rope.inv_freq);
+  const TmaPlan plan = plan_tma(heads, num_tokens);
+  if (plan.stage_bytes != 0) {
+    // staged kernel: persistent, as many CTAs as fit on the SMs
+    // the shared-memory opt-in is a per-device attribute of the kernel
+    static bool smem_set[64] = {};
+    const int smem = static_cast<int>(kStages * plan.stage_bytes + 2 * kStages * 8);
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+      return set_error(VJ_ERR_CUDA, "vj_kv_store_qknorm_rope: cudaGetDevice failed");
+    }
+    if (dev < 0 || dev >= 64 || !smem_set[dev]) {
+      if (cudaFuncSetAttribute(kv_store_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               200 * 1024) != cudaSuccess) {
+        return set_error(VJ_ERR_CUDA, "vj_kv_store_qknorm_rope: cudaFuncSetAttribute failed");
+      }
+      if (dev >= 0 && dev < 64) smem_set[dev] = true;
+    }
+    const int per_sm = std::max(1, (227 * 1024) / (smem + 1024));
+    const int64_t cap = static_cast<int64_t>(num_sms()) * per_sm;
+    a.t_begin = 0;
+    a.num_rows = 0;
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(plan.num_units, cap));
+    kv_store_tma_kernel<<<grid, kTmaThreads, smem, stream>>>(a, plan, num_tokens);
+    return check_launch("vj_kv_store_qknorm_rope");
+  }
+  // register kernel for head counts whose stages do not fit in shared memory.
   // __umulhi(r, magic) == r / heads exactly while r * heads < 2^32 (the
   // magic's excess over 2^32 / heads is below 1): launch in token ranges
   // that keep every row index within that bound

@@ -112,6 +112,16 @@ VJ_DEV void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar,
       : "memory");
 }
 
+// Untiled bulk copy global -> this CTA's shared memory (no multicast):
+// dst, src 16-byte aligned, bytes a multiple of 16; completion counted on bar.
+VJ_DEV void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+      "[%3];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // ----------------------------------------------------------------------------
 // ldmatrix / mma.sync (decode path: tiny GQA tiles)
 // ----------------------------------------------------------------------------

@@ -30,6 +30,7 @@ PROTOTYPES: dict[str, tuple] = {
         c_vp, c_i32,                                # rope_table, rope_table_len
         c_f32, c_f32, c_i32, c_vp]),                # eps, theta, flags, stream
     "vj_rope_table_bytes": (c_sz, [c_i32, c_i32]),
+    "vj_kv_store_timeouts": (c_int, [c_vp, c_i32]),
     "vj_rope_table_build": (c_int, [c_vp, c_i32, c_i32, c_f32, c_vp]),
     "vj_paged_decode_workspace_size": (c_sz, [c_i32, c_i32, c_i32, c_i32]),
     "vj_paged_decode": (c_int, [
