@@ -180,9 +180,12 @@ VJ_API vj_status vj_paged_decode_planned(
  * (vj_paged_decode_noalloc_scratch_bytes()) that every GPU loading this
  * library keeps until the process exits. Shapes whose scratch does not fit
  * (batch must stay below ~16 MiB / (Hq * 520 B), e.g. < 1008 sequences at
- * Hq = 32) return VJ_ERR_UNSUPPORTED. The first call on each device looks
- * up the array's device address (cudaGetSymbolAddress); make that first call
- * before any stream capture. All calls on a device share the array and it
+ * Hq = 32) return VJ_ERR_UNSUPPORTED. Its split budget (about 1008 - batch
+ * chunks at Hq = 32, against 4096 + batch with a default workspace) allows
+ * fewer splits, so batches of few long sequences run slower than through
+ * vj_paged_decode. The first call in each CUDA context (each device, with
+ * the runtime's primary contexts) looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture. All calls on a device share the array and it
  * keeps the last call's contents (every word a call reads is rewritten by
  * that call first); calls whose kernels overlap on the GPU race on it, so
  * order them on one stream. It allocates nothing.

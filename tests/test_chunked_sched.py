@@ -233,3 +233,21 @@ def test_prefix_cache_invariants_under_pressure():
     assert all(r.num_completion_tokens == r.max_new_tokens for r in reqs)
     assert len(kv.free_block_queue) == kv.num_blocks
     assert sched.prefix_hit_tokens > 0
+
+
+def test_prefix_cache_hash_collision_is_not_a_hit():
+    """A cached block is reused only if its tokens and its parent key match,
+    not on the hash alone: force every chained hash to collide and check that
+    a different prompt gets no hit while the same prompt still does."""
+    kv, sched = _prefix_setup()
+    kv.block_hashes = lambda token_ids, n, known=None: [7 + i for i in range(n)]
+    p = list(range(200, 264))                              # 4 full blocks
+    r1 = _req(p, new=1)
+    sched.add(r1)
+    while not sched.is_finished():
+        _step(sched)
+    assert len(kv.lookup_prefix(_req(p), 10)) == 4        # same tokens: hit
+    other = list(range(900, 964))                          # same (forced) keys, other tokens
+    assert kv.lookup_prefix(_req(other), 10) == []
+    mixed = p[:32] + other[32:]                            # first two blocks match only
+    assert len(kv.lookup_prefix(_req(mixed), 10)) == 2

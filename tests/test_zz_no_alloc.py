@@ -4,9 +4,10 @@ A caller like an XLA/JAX custom-call handler cannot cudaMalloc (the runtime
 owns device memory), so this entry point keeps its scratch in a fixed device
 array instead of a caller workspace. These tests call it through the C ABI
 (ctypes, no torch wrapper) and check, on two calls in a row, that it matches
-the workspace entry point vj_paged_decode within the decode tolerance
-(max-abs 2e-2, mean-abs 2e-3), and that oversized shapes are rejected.
-The file is named to be collected last."""
+the workspace entry point vj_paged_decode and the CPU oracle
+(oracle.attention.decode_attention) within the decode tolerance (max-abs
+2e-2, mean-abs 2e-3), and that oversized shapes are rejected. The file is
+named to be collected last.""" 
 import ctypes
 import math
 
@@ -14,6 +15,7 @@ import numpy as np
 import pytest
 import torch
 
+from oracle import attention as oatt
 from oracle.bf16 import bf16
 
 pytestmark = pytest.mark.gpu
@@ -37,7 +39,8 @@ def _case(B, Hq, Hkv, bs, seed):
     q = bf16(rng.standard_normal((B, Hq, 128)))
     cache = bf16(rng.standard_normal((2, nb, bs, Hkv, 128)))
     t = lambda x, dt=torch.bfloat16: torch.from_numpy(np.ascontiguousarray(x)).to(dt).cuda()
-    return t(q), t(cache), t(bt, torch.int32), t(lens, torch.int32)
+    oracle = oatt.decode_attention(q, cache[0], cache[1], bt, lens, 1.0 / math.sqrt(128))
+    return t(q), t(cache), t(bt, torch.int32), t(lens, torch.int32), oracle
 
 
 def _args(q, cache, bt, lens, out):
@@ -53,7 +56,7 @@ def _args(q, cache, bt, lens, out):
 def test_noalloc_matches_workspace_decode_twice(B, Hq, Hkv, bs):
     from vllm_b200 import _native
     lib = _native.load()
-    q, cache, bt, lens = _case(B, Hq, Hkv, bs, seed=B + Hq)
+    q, cache, bt, lens, oracle = _case(B, Hq, Hkv, bs, seed=B + Hq)
     stream = torch.cuda.current_stream().cuda_stream
 
     ref = torch.empty_like(q)
@@ -71,8 +74,9 @@ def test_noalloc_matches_workspace_decode_twice(B, Hq, Hkv, bs):
     for out in outs:
         o = out.float().cpu().numpy()
         assert np.isfinite(o).all()
-        err = np.abs(o - r)
-        assert err.max() <= MAX_ABS and err.mean() <= MEAN_ABS, (err.max(), err.mean())
+        for want in (r, oracle):
+            err = np.abs(o - want)
+            assert err.max() <= MAX_ABS and err.mean() <= MEAN_ABS, (err.max(), err.mean())
     assert np.all(outs[0].float().cpu().numpy()[0] == 0)   # length-0 sequence
 
 

@@ -491,6 +491,13 @@ vj_status decode_impl(
   if (g > 8) {
     return set_error(VJ_ERR_UNSUPPORTED, "vj_paged_decode: at most 8 query heads per KV head");
   }
+  // the chunk kernel's stage words pack (kv head, chunk) as h | chunk << 8
+  if (num_kv_heads > 255) {
+    return set_error(VJ_ERR_UNSUPPORTED, "vj_paged_decode: at most 255 KV heads");
+  }
+  if (max_chunks >= (1 << 23)) {
+    return set_error(VJ_ERR_UNSUPPORTED, "vj_paged_decode: max_chunks must be below 2^23");
+  }
   if (block_size <= 0 || block_size % kPageTok != 0) {
     return set_error(VJ_ERR_UNSUPPORTED, "vj_paged_decode: block_size must be a multiple of 16");
   }
@@ -587,34 +594,64 @@ namespace {
 constexpr size_t kStaticScratchBytes = size_t(16) << 20;  // 16 MiB per device
 __device__ __align__(256) uint8_t g_decode_scratch[kStaticScratchBytes];
 
-constexpr int kMaxDevices = 64;
+// The array's address belongs to a CUDA context (a module is loaded per
+// context), so the cache is keyed by the current context; with the runtime's
+// primary contexts that is once per device. The lookup makes no allocation.
+constexpr int kMaxContexts = 128;
 std::mutex g_scratch_mu;
-void *g_scratch_dev_ptr[kMaxDevices] = {nullptr};
+struct ScratchEntry {
+  CUcontext ctx;
+  void *ptr;
+};
+ScratchEntry g_scratch_cache[kMaxContexts];
+int g_scratch_entries = 0;
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+CtxGetCurrentFn g_ctx_get_current = nullptr;
 
-// Device address of g_decode_scratch on the current device. In host code the
+// Device address of g_decode_scratch in the current context. In host code the
 // symbol only names a host-side stand-in, so the address is looked up once
-// per device (with that device current) and cached.
+// per context (with it current) and cached.
 int scratch_address(void **ptr) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) {
-    return set_error(VJ_ERR_CUDA, std::string("vj_paged_decode_noalloc: cudaGetDevice: ") +
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_ctx_get_current == nullptr) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || fn == nullptr) {
+      return set_error(VJ_ERR_CUDA, "vj_paged_decode_noalloc: cuCtxGetCurrent not found");
+    }
+    g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+  }
+  CUcontext ctx = nullptr;
+  void *p = nullptr;
+  cudaError_t e = cudaSuccess;
+  if (g_ctx_get_current(&ctx) != CUDA_SUCCESS) {
+    return set_error(VJ_ERR_CUDA, "vj_paged_decode_noalloc: cuCtxGetCurrent failed");
+  }
+  if (ctx == nullptr) {
+    // no context on this thread yet: the runtime call below creates and binds
+    // the device's primary context
+    e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess || g_ctx_get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) {
+      return set_error(VJ_ERR_CUDA, "vj_paged_decode_noalloc: no CUDA context");
+    }
+  }
+  for (int i = 0; i < g_scratch_entries; ++i) {
+    if (g_scratch_cache[i].ctx == ctx) {
+      *ptr = g_scratch_cache[i].ptr;
+      return VJ_OK;
+    }
+  }
+  if (g_scratch_entries == kMaxContexts) {
+    return set_error(VJ_ERR_UNSUPPORTED, "vj_paged_decode_noalloc: too many CUDA contexts");
+  }
+  if (p == nullptr) e = cudaGetSymbolAddress(&p, g_decode_scratch);
+  if (e != cudaSuccess || p == nullptr) {
+    return set_error(VJ_ERR_CUDA, std::string("vj_paged_decode_noalloc: cudaGetSymbolAddress: ") +
                                       cudaGetErrorString(e));
   }
-  if (dev < 0 || dev >= kMaxDevices) {
-    return set_error(VJ_ERR_UNSUPPORTED, "vj_paged_decode_noalloc: device index out of range");
-  }
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_dev_ptr[dev] == nullptr) {
-    void *p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_decode_scratch);
-    if (e != cudaSuccess || p == nullptr) {
-      return set_error(VJ_ERR_CUDA, std::string("vj_paged_decode_noalloc: cudaGetSymbolAddress: ") +
-                                        cudaGetErrorString(e));
-    }
-    g_scratch_dev_ptr[dev] = p;
-  }
-  *ptr = g_scratch_dev_ptr[dev];
+  g_scratch_cache[g_scratch_entries++] = {ctx, p};
+  *ptr = p;
   return VJ_OK;
 }
 }  // namespace

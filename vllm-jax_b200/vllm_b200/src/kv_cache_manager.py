@@ -23,6 +23,11 @@ class Block:
     block_id: int
     ref_count: int
     hash: int | None = None   # prefix-cache key of a full block (None: not cached)
+    # what the key stands for, compared on every hit so that a hash collision
+    # can never hand out another prompt's KV: the block's tokens and the key
+    # of the block before it in its request (0 for the first block)
+    tokens: tuple | None = None
+    parent: int = 0
 
 
 class FreeBlockQueue:
@@ -87,6 +92,8 @@ class KVCacheManager:
             if self.cached.get(block.hash) is block:
                 del self.cached[block.hash]
             block.hash = None
+            block.tokens = None
+            block.parent = 0
         block.ref_count += 1
         table.append(block)
 
@@ -133,14 +140,17 @@ class KVCacheManager:
 
     def lookup_prefix(self, request: Request, max_blocks: int) -> list[Block]:
         """Cached blocks holding the longest prefix of the request's full blocks."""
-        hashes = self.block_hashes(request.token_ids, min(max_blocks,
-                                                          len(request) // self.block_size))
+        bs = self.block_size
+        hashes = self.block_hashes(request.token_ids, min(max_blocks, len(request) // bs))
         hit = []
-        for h in hashes:
+        parent = 0
+        for i, h in enumerate(hashes):
             b = self.cached.get(h)
-            if b is None:
+            if (b is None or b.parent != parent
+                    or b.tokens != tuple(request.token_ids[i * bs:(i + 1) * bs])):
                 break
             hit.append(b)
+            parent = h
         return hit
 
     def acquire(self, request: Request, blocks: list[Block]) -> None:
@@ -164,10 +174,13 @@ class KVCacheManager:
             return
         chain = self.block_hashes(request.token_ids, full, known)
         request.block_hash_chain = chain
+        bs = self.block_size
         for i in range(len(known), full):
             b = table[i]
             if b.hash is None and chain[i] not in self.cached:
                 b.hash = chain[i]
+                b.tokens = tuple(request.token_ids[i * bs:(i + 1) * bs])
+                b.parent = chain[i - 1] if i else 0
                 self.cached[chain[i]] = b
 
     def deallocate(self, request: Request) -> None:
