@@ -692,7 +692,7 @@ def run_prefill(args, rank, world, local_rank):
 
 
 # ncu capture of decode_chunk_kernel on the first 48 C3 sequences (402,759
-# context tokens; profiles/decode_chunk_kernel_c3.md): dram read + write bytes.
+# context tokens): dram read + write bytes.
 # DRAM traffic grows with the context tokens streamed, so a full C3 launch is
 # scaled by its context-token count.
 DECODE_PROFILE = {"ctx_tokens": 402_759, "dram_bytes": 1_651_833_000 + 23_638_016}
