@@ -696,8 +696,8 @@ def run_prefill(args, rank, world, local_rank):
 # DRAM traffic grows with the context tokens streamed, so a full C3 launch is
 # scaled by its context-token count.
 DECODE_PROFILE = {"ctx_tokens": 402_759, "dram_bytes": 1_651_833_000 + 23_638_016}
-# K3 (kv_store_qknorm_rope_kernel) on the first 16 C2 sequences, 34,069 tokens
-KVSTORE_PROFILE = {"tokens": 34_069, "dram_bytes": 419_022_592 + 374_849_536}
+# K3 (kv_store_tma_kernel) on the first 16 C2 sequences, 34,069 tokens
+KVSTORE_PROFILE = {"tokens": 34_069, "dram_bytes": 424_025_344 + 367_532_544}
 
 
 def decode_traffic(ctx_tokens: int) -> int:

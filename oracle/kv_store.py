@@ -53,22 +53,23 @@ def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
 
 def rmsnorm_head(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
     """flax RMSNorm over a 128-dim head row with the sum of squares taken in
-    fp32 in the order vj_kv_store_qknorm_rope uses: lane l of 16 owns dims
-    8l..8l+7 and sums its even dims and its odd dims in dim order, adds the
-    two, then lanes combine by a butterfly (xor 8, 4, 2, 1). bf16 squares are
-    exact in fp32, so only the order of the additions is a choice (XLA's
-    reduction order is not observable here)."""
+    fp32 in the order vj_kv_store_qknorm_rope uses: lane l of 8 owns dims
+    [8l, 8l+8) and [64+8l, 64+8l+8), sums the even dims and the odd dims of
+    those 16 in that order, adds the two, then lanes combine by a butterfly
+    (xor 4, 2, 1). bf16 squares are exact in fp32, so only the order of the
+    additions is a choice (XLA's reduction order is not observable here)."""
     x = np.asarray(x, np.float32)
     D = x.shape[-1]
-    sq = (x * x).reshape(*x.shape[:-1], D // 8, 8)
+    halves = (x * x).reshape(*x.shape[:-1], 2, 8, D // 16)       # [half, lane, 8 dims]
+    sq = np.swapaxes(halves, -3, -2).reshape(*x.shape[:-1], 8, D // 8)   # [lane, 16 dims]
     se = sq[..., 0]
     so = sq[..., 1]
-    for j in (2, 4, 6):
-        se = (se + sq[..., j]).astype(np.float32)
-        so = (so + sq[..., j + 1]).astype(np.float32)
+    for j in range(1, D // 16):
+        se = (se + sq[..., 2 * j]).astype(np.float32)
+        so = (so + sq[..., 2 * j + 1]).astype(np.float32)
     lane = (se + so).astype(np.float32)
-    idx = np.arange(D // 8)
-    for o in (8, 4, 2, 1):
+    idx = np.arange(8)
+    for o in (4, 2, 1):
         lane = (lane + lane[..., idx ^ o]).astype(np.float32)
     ss = lane[..., :1]
     ms = (ss * np.float32(1.0 / D)).astype(np.float32)

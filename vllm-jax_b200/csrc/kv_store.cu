@@ -38,8 +38,6 @@ namespace {
 constexpr int kThreads = 256;      // 16 half-warps
 constexpr int kHeadDim = 128;
 constexpr int kPairs = kHeadDim / 2;
-constexpr int kRowsPerHw = 4;      // rows in flight per half-warp
-constexpr int kRowsPerCta = 16 * kRowsPerHw;
 // bf16x2 word (lo = -1.0, hi = +1.0)
 constexpr uint32_t kMinusPlusOne = 0x3F80BF80u;
 // bf16(1/sqrt(128)) in both halves (prefill_paged_attention.py:60)
@@ -150,157 +148,178 @@ rope_table_kernel(uint32_t *table, int num_positions, RopeTable rope) {
   }
 }
 
-// Norm (optional) + RoPE (optional) + q scaling (optional) of one 8-element
-// lane slice `wd` of a q or k row.
-VJ_DEV void norm_rope_slice(uint32_t (&wd)[4], const uint32_t (&w)[4], const uint4 &tab,
-                            uint32_t half_mask, float eps, bool do_norm, bool do_rope,
-                            int qscale) {
+// Row layout shared by both kernels: 8 lanes own one 128-dim row; lane l8
+// holds dims [8*l8, 8*l8+8) and [64+8*l8, 64+8*l8+8) as 8 bf16x2 words, so
+// each of the row's two 128-byte halves is one conflict-free shared-memory
+// access and one coalesced global access per lane group.
+struct RowSlice {
+  uint32_t w[8];
+};
+
+VJ_DEV RowSlice load_slice(const void *row, int l8) {
+  const uint4 a = *reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(row) + l8 * 16);
+  const uint4 b =
+      *reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(row) + 128 + l8 * 16);
+  return {{a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w}};
+}
+VJ_DEV RowSlice ldg_slice(const __nv_bfloat16 *row, int l8) {
+  const uint4 a = __ldcs(reinterpret_cast<const uint4 *>(row + l8 * 8));
+  const uint4 b = __ldcs(reinterpret_cast<const uint4 *>(row + 64 + l8 * 8));
+  return {{a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w}};
+}
+VJ_DEV RowSlice ldg_nc_slice(const __nv_bfloat16 *row, int l8) {
+  const uint4 a = __ldg(reinterpret_cast<const uint4 *>(row + l8 * 8));
+  const uint4 b = __ldg(reinterpret_cast<const uint4 *>(row + 64 + l8 * 8));
+  return {{a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w}};
+}
+VJ_DEV void stg_slice(__nv_bfloat16 *row, int l8, const RowSlice &v, bool streaming) {
+  const uint4 a = make_uint4(v.w[0], v.w[1], v.w[2], v.w[3]);
+  const uint4 b = make_uint4(v.w[4], v.w[5], v.w[6], v.w[7]);
+  if (streaming) {
+    __stcs(reinterpret_cast<uint4 *>(row + l8 * 8), a);
+    __stcs(reinterpret_cast<uint4 *>(row + 64 + l8 * 8), b);
+  } else {
+    *reinterpret_cast<uint4 *>(row + l8 * 8) = a;
+    *reinterpret_cast<uint4 *>(row + 64 + l8 * 8) = b;
+  }
+}
+// (cos, sin) words of the lane's 8 pairs at `position`, computed (positions
+// past the end of the table)
+VJ_DEV RowSlice rope_slice(int position, const RopeTable &rope, int l8) {
+  RowSlice c;
+#pragma unroll 1
+  for (int j = 0; j < 8; ++j) {
+    const int pair = (j < 4 ? 0 : 32) + l8 * 4 + (j & 3);
+    c.w[j] = rope_word(position, rope.inv_freq[pair]);
+  }
+  return c;
+}
+
+// Norm (optional) + RoPE (optional) + q scaling (optional) of one lane's
+// slice of a q or k row. The row's sum of squares is exact per bf16 square
+// and summed in fp32: per lane, even and odd dims separately in word order,
+// then their sum, then a butterfly over the group's 8 lanes (xor 4, 2, 1).
+VJ_DEV void norm_rope_row(RowSlice &x, const RowSlice &w, const RowSlice &cs, unsigned grp_mask,
+                          float eps, bool do_norm, bool do_rope, int qscale) {
   if (do_norm) {
-    uint64_t xp[4];
+    uint64_t xp[8];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) xp[j] = unpack_f32x2(wd[j]);
-    // per lane: (sum of even dims, sum of odd dims) in dim order, in fp32
+    for (int j = 0; j < 8; ++j) xp[j] = unpack_f32x2(x.w[j]);
     uint64_t s2 = f32x2_mul(xp[0], xp[0]);
 #pragma unroll
-    for (int j = 1; j < 4; ++j) s2 = f32x2_fma(xp[j], xp[j], s2);
+    for (int j = 1; j < 8; ++j) s2 = f32x2_fma(xp[j], xp[j], s2);
     float se, so;
     f32x2_split(s2, se, so);
     float ss = __fadd_rn(se, so);
-    // butterfly over the half-warp's 16 lanes (its two halves may hold rows
-    // of different kinds, so the mask is the half-warp)
 #pragma unroll
-    for (int o = 8; o >= 1; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(half_mask, ss, o));
+    for (int o = 4; o >= 1; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(grp_mask, ss, o));
     // flax RMSNorm: y = bf16(x * (rsqrt(mean(x^2) + eps) * scale)); mean = sum / 128
     // is a power-of-two scale, exact as a multiply
     const float ms = __fmul_rn(ss, 1.0f / kHeadDim);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
     const uint64_t inv2 = f32x2(inv, inv);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint64_t m = f32x2_mul(inv2, unpack_f32x2(w[j]));
+    for (int j = 0; j < 8; ++j) {
+      const uint64_t m = f32x2_mul(inv2, unpack_f32x2(w.w[j]));
       float y0, y1;
       f32x2_split(f32x2_mul(xp[j], m), y0, y1);
-      wd[j] = cvt_bf16x2(y0, y1);
+      x.w[j] = cvt_bf16x2(y0, y1);
     }
   }
   if (do_rope) {
-    const uint32_t cs[4] = {tab.x, tab.y, tab.z, tab.w};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < 8; ++j) {
       // pair (x1, x2) = word j; stack((x1*cos - x2*sin, x1*sin + x2*cos), -1)
-      const uint32_t p = bf16x2_mul(wd[j], cs[j]);                     // (x1 c, x2 s)
-      const uint32_t q = bf16x2_mul(wd[j], prmt(cs[j], cs[j], 0x1032)); // (x1 s, x2 c)
-      const uint32_t u = prmt(p, q, 0x5410);                           // (x1 c, x1 s)
-      const uint32_t v = prmt(p, q, 0x7632);                           // (x2 s, x2 c)
-      wd[j] = bf16x2_fma(v, kMinusPlusOne, u);
+      const uint32_t p = bf16x2_mul(x.w[j], cs.w[j]);                       // (x1 c, x2 s)
+      const uint32_t q = bf16x2_mul(x.w[j], prmt(cs.w[j], cs.w[j], 0x1032)); // (x1 s, x2 c)
+      const uint32_t u = prmt(p, q, 0x5410);                                // (x1 c, x1 s)
+      const uint32_t v = prmt(p, q, 0x7632);                                // (x2 s, x2 c)
+      x.w[j] = bf16x2_fma(v, kMinusPlusOne, u);
     }
   }
   if (qscale == VJ_KV_QSCALE_MUL_RSQRT_D) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) wd[j] = bf16x2_mul(wd[j], kRsqrtDx2);
+    for (int j = 0; j < 8; ++j) x.w[j] = bf16x2_mul(x.w[j], kRsqrtDx2);
   } else if (qscale == VJ_KV_QSCALE_DIV_SQRT_D) {
     // bf16(x / 11.3125) for every bf16 x equals bf16(fp32(x * fp32(1/11.3125)))
     // (checked exhaustively over all finite bf16 values)
     const uint64_t r2 = f32x2(1.0f / 11.3125f, 1.0f / 11.3125f);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < 8; ++j) {
       float y0, y1;
-      f32x2_split(f32x2_mul(unpack_f32x2(wd[j]), r2), y0, y1);
-      wd[j] = cvt_bf16x2(y0, y1);
+      f32x2_split(f32x2_mul(unpack_f32x2(x.w[j]), r2), y0, y1);
+      x.w[j] = cvt_bf16x2(y0, y1);
     }
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 3)
+// Store one finished row: q rows to q_out, k/v rows to their cache slot
+// (and k rows to k_out when given).
+VJ_DEV void store_row(const KvArgs &a, int64_t t, int h, int64_t slot, const RowSlice &v,
+                      int l8) {
+  if (h < a.Hq) {
+    stg_slice(a.q_out + (t * a.Hq + h) * kHeadDim, l8, v, true);
+    return;
+  }
+  const bool is_k = h < a.Hq + a.Hkv;
+  const int hk = is_k ? h - a.Hq : h - a.Hq - a.Hkv;
+  if (is_k && a.k_out != nullptr) stg_slice(a.k_out + (t * a.Hkv + hk) * kHeadDim, l8, v, false);
+  if (slot < 0 && (a.flags & VJ_KV_WRAP_NEGATIVE)) slot += a.num_slots;
+  if (slot < 0 || slot >= a.num_slots) return;  // mode="drop"
+  const int64_t blk = a.bs_shift >= 0 ? slot >> a.bs_shift : slot / a.block_size;
+  const int64_t off = a.bs_shift >= 0 ? slot & (a.block_size - 1) : slot % a.block_size;
+  stg_slice((is_k ? a.k_cache : a.v_cache) + blk * a.sb + off * a.st + hk * a.sh, l8, v, false);
+}
+
+VJ_DEV void load_weights(const KvArgs &a, int l8, RowSlice &qw, RowSlice &kw) {
+  for (int j = 0; j < 8; ++j) qw.w[j] = kw.w[j] = 0u;
+  if (!(a.flags & VJ_KV_NORM)) return;
+  if (a.Hq > 0) qw = ldg_nc_slice(a.q_w, l8);
+  kw = ldg_nc_slice(a.k_w, l8);
+}
+
+// Register kernel (for head counts whose staged units do not fit in shared
+// memory): 32 row groups per CTA, kRowsPerGrp rows each in flight.
+constexpr int kRowsPerGrp = 2;
+constexpr int kRowsPerCtaReg = 32 * kRowsPerGrp;
+
+__global__ void __launch_bounds__(kThreads, 2)
 kv_store_rows_kernel(const KvArgs a) {
-  const int tid = threadIdx.x;
-  const int hw = tid >> 4;     // half-warp index
-  const int l16 = tid & 15;    // lane inside the half-warp: dims 8*l16 .. +7
-  const unsigned half_mask = 0xffffu << (16 * (hw & 1));
+  const int grp = threadIdx.x >> 3;
+  const int l8 = threadIdx.x & 7;
+  const unsigned grp_mask = 0xffu << (8 * (grp & 3));
   const bool do_norm = (a.flags & VJ_KV_NORM) != 0;
   const bool do_rope = (a.flags & VJ_KV_ROPE) != 0;
   const int qscale = a.flags & (VJ_KV_QSCALE_DIV_SQRT_D | VJ_KV_QSCALE_MUL_RSQRT_D);
-  uint32_t qw[4] = {0u, 0u, 0u, 0u}, kw[4] = {0u, 0u, 0u, 0u};
-  if (do_norm) {
-    if (a.Hq > 0) {
-      const uint4 t = __ldg(reinterpret_cast<const uint4 *>(a.q_w + l16 * 8));
-      qw[0] = t.x; qw[1] = t.y; qw[2] = t.z; qw[3] = t.w;
-    }
-    const uint4 t = __ldg(reinterpret_cast<const uint4 *>(a.k_w + l16 * 8));
-    kw[0] = t.x; kw[1] = t.y; kw[2] = t.z; kw[3] = t.w;
-  }
-
-  for (uint32_t base = blockIdx.x * kRowsPerCta; base < a.num_rows;
-       base += gridDim.x * kRowsPerCta) {
-    uint4 raw[kRowsPerHw], tab[kRowsPerHw];
-    int tok[kRowsPerHw], head[kRowsPerHw], pos[kRowsPerHw];
-    // ---- 1. indices, the rows' loads and positions, all in flight together
-#pragma unroll
-    for (int k = 0; k < kRowsPerHw; ++k) {
-      const uint32_t r = base + hw + 16 * k;
-      raw[k] = make_uint4(0u, 0u, 0u, 0u);
-      tab[k] = make_uint4(0u, 0u, 0u, 0u);
-      tok[k] = -1;
-      head[k] = 0;
-      pos[k] = 0;
-      if (r < a.num_rows) {
-        const uint32_t tl = __umulhi(r, a.heads_magic);   // r / heads (host-checked range)
-        const int h = static_cast<int>(r - tl * a.heads);
-        const int64_t t = a.t_begin + tl;
-        tok[k] = static_cast<int>(tl);
-        head[k] = h;
-        const __nv_bfloat16 *src =
-            h < a.Hq ? a.q_in + t * a.qrs + h * kHeadDim
-            : h < a.Hq + a.Hkv ? a.k_in + t * a.krs + (h - a.Hq) * kHeadDim
-                               : a.v_in + t * a.vrs + (h - a.Hq - a.Hkv) * kHeadDim;
-        raw[k] = __ldcs(reinterpret_cast<const uint4 *>(src + l16 * 8));
-        if (do_rope && h < a.Hq + a.Hkv) pos[k] = __ldg(a.positions + t);
-      }
-    }
-    // ---- 2. cos/sin of the q/k rows' positions (table, or computed past its end)
-    if (do_rope) {
-#pragma unroll
-      for (int k = 0; k < kRowsPerHw; ++k) {
-        if (tok[k] < 0 || head[k] >= a.Hq + a.Hkv) continue;
-        if (pos[k] >= 0 && pos[k] < a.table_len) {
-          tab[k] = __ldg(a.rope_table + static_cast<int64_t>(pos[k]) * 16 + l16);
-        } else {
-          tab[k].x = rope_word(pos[k], a.rope.inv_freq[l16 * 4 + 0]);
-          tab[k].y = rope_word(pos[k], a.rope.inv_freq[l16 * 4 + 1]);
-          tab[k].z = rope_word(pos[k], a.rope.inv_freq[l16 * 4 + 2]);
-          tab[k].w = rope_word(pos[k], a.rope.inv_freq[l16 * 4 + 3]);
+  RowSlice qw, kw;
+  load_weights(a, l8, qw, kw);
+  for (uint32_t base = blockIdx.x * kRowsPerCtaReg; base < a.num_rows;
+       base += gridDim.x * kRowsPerCtaReg) {
+#pragma unroll 1
+    for (int k = 0; k < kRowsPerGrp; ++k) {
+      const uint32_t r = base + grp + 32 * k;
+      if (r >= a.num_rows) break;
+      const uint32_t tl = __umulhi(r, a.heads_magic);   // r / heads (host-checked range)
+      const int h = static_cast<int>(r - tl * a.heads);
+      const int64_t t = a.t_begin + tl;
+      const __nv_bfloat16 *src =
+          h < a.Hq ? a.q_in + t * a.qrs + h * kHeadDim
+          : h < a.Hq + a.Hkv ? a.k_in + t * a.krs + (h - a.Hq) * kHeadDim
+                             : a.v_in + t * a.vrs + (h - a.Hq - a.Hkv) * kHeadDim;
+      RowSlice x = ldg_slice(src, l8);
+      if (h < a.Hq + a.Hkv) {
+        RowSlice cs{};
+        if (do_rope) {
+          const int pos = __ldg(a.positions + t);
+          cs = (pos >= 0 && pos < a.table_len)
+                   ? ldg_nc_slice(reinterpret_cast<const __nv_bfloat16 *>(
+                                      a.rope_table + static_cast<int64_t>(pos) * 16), l8)
+                   : rope_slice(pos, a.rope, l8);
         }
+        norm_rope_row(x, h < a.Hq ? qw : kw, cs, grp_mask, a.eps, do_norm, do_rope,
+                      h < a.Hq ? qscale : 0);
       }
-    }
-    // ---- 3. norm, rope, stores
-#pragma unroll
-    for (int k = 0; k < kRowsPerHw; ++k) {
-      if (tok[k] < 0) continue;
-      const int h = head[k];
-      const int64_t t = a.t_begin + tok[k];
-      uint32_t wd[4] = {raw[k].x, raw[k].y, raw[k].z, raw[k].w};
-      if (h < a.Hq) {
-        norm_rope_slice(wd, qw, tab[k], half_mask, a.eps, do_norm, do_rope, qscale);
-        __stcs(reinterpret_cast<uint4 *>(a.q_out + (t * a.Hq + h) * kHeadDim + l16 * 8),
-               make_uint4(wd[0], wd[1], wd[2], wd[3]));
-        continue;
-      }
-      const bool is_k = h < a.Hq + a.Hkv;
-      const int hk = is_k ? h - a.Hq : h - a.Hq - a.Hkv;
-      if (is_k) {
-        norm_rope_slice(wd, kw, tab[k], half_mask, a.eps, do_norm, do_rope, 0);
-        if (a.k_out != nullptr) {
-          *reinterpret_cast<uint4 *>(a.k_out + (t * a.Hkv + hk) * kHeadDim + l16 * 8) =
-              make_uint4(wd[0], wd[1], wd[2], wd[3]);
-        }
-      }
-      int64_t slot = __ldg(a.slots + t);
-      if (slot < 0 && (a.flags & VJ_KV_WRAP_NEGATIVE)) slot += a.num_slots;
-      if (slot < 0 || slot >= a.num_slots) continue;  // mode="drop"
-      const int64_t blk = a.bs_shift >= 0 ? slot >> a.bs_shift : slot / a.block_size;
-      const int64_t off = a.bs_shift >= 0 ? slot & (a.block_size - 1) : slot % a.block_size;
-      __nv_bfloat16 *dst = (is_k ? a.k_cache : a.v_cache) + blk * a.sb + off * a.st + hk * a.sh;
-      *reinterpret_cast<uint4 *>(dst + l16 * 8) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+      store_row(a, t, h, h < a.Hq ? 0 : __ldg(a.slots + t), x, l8);
     }
   }
 }
@@ -311,9 +330,9 @@ kv_store_rows_kernel(const KvArgs a) {
 // ring. One producer thread loads a unit's positions and slots, then issues
 // untiled bulk copies (cp.async.bulk, no multicast) of its q, k and v rows and
 // of its tokens' (cos, sin) table rows, counted on the stage's full barrier;
-// 8 consumer warps (16 half-warps, one row each at a time) normalise, rotate,
-// scale and store, then release the stage. Loads of later units are in flight
-// while a unit is computed, so HBM stays busy with few registers per thread.
+// 8 consumer warps (32 row groups of 8 lanes) normalise, rotate, scale and
+// store, then release the stage. Loads of later units are in flight while a
+// unit is computed, so HBM stays busy with few registers per thread.
 // Every wait is bounded (2 s); a timed-out wait counts in g_kv_store_timeouts
 // and the CTA drains its copies in flight and returns.
 // ---------------------------------------------------------------------------
@@ -331,7 +350,9 @@ struct TmaPlan {
   int64_t num_units;
 };
 
-__global__ void __launch_bounds__(kTmaThreads, 1)
+// 9 warps of 2 CTAs share an SM: 5 warps on one sub-partition must fit its
+// 16K registers, so at most 96 (allocated in steps of 8) per thread
+__global__ void __maxnreg__(96)
 kv_store_tma_kernel(const KvArgs a, const TmaPlan p, int64_t num_tokens) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * p.stage_bytes);
@@ -397,19 +418,12 @@ kv_store_tma_kernel(const KvArgs a, const TmaPlan p, int64_t num_tokens) {
   }
 
   // -------------------------------------------------------------- consumers
-  const int hw = threadIdx.x >> 4;   // 0..15
-  const int l16 = threadIdx.x & 15;
-  const unsigned half_mask = 0xffffu << (16 * (hw & 1));
+  const int grp = threadIdx.x >> 3;   // 0..31
+  const int l8 = threadIdx.x & 7;
+  const unsigned grp_mask = 0xffu << (8 * (grp & 3));
   const int qscale = a.flags & (VJ_KV_QSCALE_DIV_SQRT_D | VJ_KV_QSCALE_MUL_RSQRT_D);
-  uint32_t qw[4] = {0u, 0u, 0u, 0u}, kw[4] = {0u, 0u, 0u, 0u};
-  if (do_norm) {
-    if (a.Hq > 0) {
-      const uint4 t = __ldg(reinterpret_cast<const uint4 *>(a.q_w + l16 * 8));
-      qw[0] = t.x; qw[1] = t.y; qw[2] = t.z; qw[3] = t.w;
-    }
-    const uint4 t = __ldg(reinterpret_cast<const uint4 *>(a.k_w + l16 * 8));
-    kw[0] = t.x; kw[1] = t.y; kw[2] = t.z; kw[3] = t.w;
-  }
+  RowSlice qw, kw;
+  load_weights(a, l8, qw, kw);
   int64_t it = 0;
   for (int64_t u = blockIdx.x; u < p.num_units; u += gridDim.x, ++it) {
     const int stage = static_cast<int>(it % kStages);
@@ -422,46 +436,21 @@ kv_store_tma_kernel(const KvArgs a, const TmaPlan p, int64_t num_tokens) {
     const int64_t t0 = u * p.G;
     const int ng = static_cast<int>(num_tokens - t0 < p.G ? num_tokens - t0 : p.G);
     const uint32_t nrows = static_cast<uint32_t>(ng) * a.heads;
-    for (uint32_t r = hw; r < nrows; r += 16) {
+    for (uint32_t r = grp; r < nrows; r += 32) {
       const int g = static_cast<int>(__umulhi(r, a.heads_magic));   // r / heads
       const int h = static_cast<int>(r - static_cast<uint32_t>(g) * a.heads);
-      const int64_t t = t0 + g;
-      const uint4 raw = *reinterpret_cast<const uint4 *>(base + p.rows_off + r * 256u + l16 * 16u);
-      uint32_t wd[4] = {raw.x, raw.y, raw.z, raw.w};
-      const bool is_q = h < a.Hq, is_k = !is_q && h < a.Hq + a.Hkv;
-      if (is_q || is_k) {
-        uint4 tab = make_uint4(0u, 0u, 0u, 0u);
+      RowSlice x = load_slice(base + p.rows_off + r * 256u, l8);
+      if (h < a.Hq + a.Hkv) {
+        RowSlice cs{};
         if (do_rope) {
           const int pos = meta[g].x;
-          if (pos >= 0 && pos < a.table_len) {
-            tab = *reinterpret_cast<const uint4 *>(base + p.tab_off + g * 256u + l16 * 16u);
-          } else {
-            tab.x = rope_word(pos, a.rope.inv_freq[l16 * 4 + 0]);
-            tab.y = rope_word(pos, a.rope.inv_freq[l16 * 4 + 1]);
-            tab.z = rope_word(pos, a.rope.inv_freq[l16 * 4 + 2]);
-            tab.w = rope_word(pos, a.rope.inv_freq[l16 * 4 + 3]);
-          }
+          cs = (pos >= 0 && pos < a.table_len) ? load_slice(base + p.tab_off + g * 256u, l8)
+                                                : rope_slice(pos, a.rope, l8);
         }
-        norm_rope_slice(wd, is_q ? qw : kw, tab, half_mask, a.eps, do_norm, do_rope,
-                        is_q ? qscale : 0);
+        norm_rope_row(x, h < a.Hq ? qw : kw, cs, grp_mask, a.eps, do_norm, do_rope,
+                      h < a.Hq ? qscale : 0);
       }
-      if (is_q) {
-        __stcs(reinterpret_cast<uint4 *>(a.q_out + (t * a.Hq + h) * kHeadDim + l16 * 8),
-               make_uint4(wd[0], wd[1], wd[2], wd[3]));
-        continue;
-      }
-      const int hk = is_k ? h - a.Hq : h - a.Hq - a.Hkv;
-      if (is_k && a.k_out != nullptr) {
-        *reinterpret_cast<uint4 *>(a.k_out + (t * a.Hkv + hk) * kHeadDim + l16 * 8) =
-            make_uint4(wd[0], wd[1], wd[2], wd[3]);
-      }
-      int64_t slot = meta[g].y;
-      if (slot < 0 && (a.flags & VJ_KV_WRAP_NEGATIVE)) slot += a.num_slots;
-      if (slot < 0 || slot >= a.num_slots) continue;  // mode="drop"
-      const int64_t blk = a.bs_shift >= 0 ? slot >> a.bs_shift : slot / a.block_size;
-      const int64_t off = a.bs_shift >= 0 ? slot & (a.block_size - 1) : slot % a.block_size;
-      __nv_bfloat16 *dst = (is_k ? a.k_cache : a.v_cache) + blk * a.sb + off * a.st + hk * a.sh;
-      *reinterpret_cast<uint4 *>(dst + l16 * 8) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+      store_row(a, t0 + g, h, meta[g].y, x, l8);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[stage]);
@@ -648,7 +637,10 @@ extern "C" vj_status vj_kv_store_qknorm_rope(
     }
     if (dev < 0 || dev >= 64 || !smem_set[dev]) {
       if (cudaFuncSetAttribute(kv_store_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               200 * 1024) != cudaSuccess) {
+                               200 * 1024) != cudaSuccess ||
+          cudaFuncSetAttribute(kv_store_tma_kernel,
+                               cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared) != cudaSuccess) {
         return set_error(VJ_ERR_CUDA, "vj_kv_store_qknorm_rope: cudaFuncSetAttribute failed");
       }
       if (dev >= 0 && dev < 64) smem_set[dev] = true;
@@ -672,7 +664,8 @@ extern "C" vj_status vj_kv_store_qknorm_rope(
     const int64_t nt = std::min(tokens_per_launch, num_tokens - t0);
     a.t_begin = t0;
     a.num_rows = static_cast<uint32_t>(nt * heads);
-    const int64_t chunks = (static_cast<int64_t>(a.num_rows) + kRowsPerCta - 1) / kRowsPerCta;
+    const int64_t chunks =
+        (static_cast<int64_t>(a.num_rows) + kRowsPerCtaReg - 1) / kRowsPerCtaReg;
     const unsigned grid = static_cast<unsigned>(std::min(chunks, grid_cap));
     kv_store_rows_kernel<<<grid, kThreads, 0, stream>>>(a);
     const vj_status st = check_launch("vj_kv_store_qknorm_rope");
