@@ -36,6 +36,9 @@ constexpr int kArThreads = 256;
 constexpr int kArCtasPerSm = 4;   // one row per CTA for decode batches up to 4 x SMs
 constexpr int kArMaxVec = 4;        // hidden <= 8 * 256 * 4 = 8192
 constexpr uint64_t kArSpinLimit = 1ull << 26;
+// at most this many rows: every rank reduces every row (one barrier) even
+// from 4 ranks on, where larger batches take the two-shot path
+constexpr int64_t kOneShotMaxRows = 64;
 
 struct ArArgs {
   const __nv_bfloat16 *bufs[VJ_TP_MAX_RANKS];  // partial of each rank (own included)
@@ -47,6 +50,7 @@ struct ArArgs {
   const __nv_bfloat16 *residual, *weight;
   __nv_bfloat16 *residual_out, *y;
   int rank, world, rows, hidden, two_shot;
+  int gmax;   // stride of the flag arrays: the largest grid (vj_tp_grid)
   float eps;
 };
 
@@ -64,7 +68,7 @@ VJ_DEV uint32_t ld_acquire_sys(const uint32_t *p) {
 // peer's announcement in mine. The release is cumulative over the CTA's
 // writes that precede the __syncthreads.
 VJ_DEV bool cta_barrier(const ArArgs &a, int set, uint32_t epoch, int *s_fail) {
-  const int b = blockIdx.x, G = gridDim.x, tid = threadIdx.x;
+  const int b = blockIdx.x, G = a.gmax, tid = threadIdx.x;
   const size_t base = (size_t)set * a.world * G;
   __syncthreads();
   if (tid < a.world && tid != a.rank) {
@@ -165,26 +169,6 @@ VJ_DEV float reduce_row(const ArArgs &a, int row, __nv_bfloat16 *res, double *re
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
 }
 
-// Two-shot gather: copy `row` of x from a peer's result buffer. Returns 1/rms.
-VJ_DEV float gather_row(const ArArgs &a, int row, const __nv_bfloat16 *src, double *red) {
-  const int H = a.hidden, nvec = H / 8, tid = threadIdx.x;
-  const size_t off = (size_t)row * H;
-  double ss = 0.0;
-#pragma unroll
-  for (int k = 0; k < kArMaxVec; ++k) {
-    const int i = tid + k * kArThreads;
-    if (i < nvec) {
-      const uint4 xv = __ldcg(reinterpret_cast<const uint4 *>(src + off) + i);
-      reinterpret_cast<uint4 *>(a.residual_out + off)[i] = xv;
-      const uint32_t o[4] = {xv.x, xv.y, xv.z, xv.w};
-      ss += sq8(o);
-    }
-  }
-  const double tot = block_sum(ss, red);
-  const float ms = __fdiv_rn(static_cast<float>(tot), static_cast<float>(H));
-  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
-}
-
 // y = bf16(x * (inv * w)) of `row`; x re-read from residual_out, where this
 // same thread wrote it.
 VJ_DEV void norm_row(const ArArgs &a, int row, float inv) {
@@ -208,12 +192,77 @@ VJ_DEV void norm_row(const ArArgs &a, int row, float inv) {
   }
 }
 
+// Sums over the block of one double per rank slot; every thread gets them.
+VJ_DEV void block_sum_ranks(double (&v)[VJ_TP_MAX_RANKS], double *red, int world) {
+  const int tid = threadIdx.x;
+#pragma unroll
+  for (int r = 0; r < VJ_TP_MAX_RANKS; ++r) {
+    if (r < world) {
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) v[r] += __shfl_xor_sync(0xffffffffu, v[r], o);
+      if ((tid & 31) == 0) red[(tid >> 5) * VJ_TP_MAX_RANKS + r] = v[r];
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < VJ_TP_MAX_RANKS; ++r) {
+    if (r < world) {
+      double t = 0.0;
+#pragma unroll
+      for (int w = 0; w < kArThreads / 32; ++w) t += red[w * VJ_TP_MAX_RANKS + r];
+      v[r] = t;
+    }
+  }
+  __syncthreads();   // red[] is rewritten by the next rows
+}
+
+// Two-shot gather: row `j` of every peer's slice (rows [p*S, p*S + S)) is
+// copied from that peer's result buffer into residual_out and normalised;
+// the loads of all peers are in flight together.
+VJ_DEV void gather_rows(const ArArgs &a, int j, int S, double *red) {
+  const int H = a.hidden, nvec = H / 8, tid = threadIdx.x;
+  double ss[VJ_TP_MAX_RANKS];
+#pragma unroll
+  for (int p = 0; p < VJ_TP_MAX_RANKS; ++p) ss[p] = 0.0;
+#pragma unroll 1
+  for (int k = 0; k < kArMaxVec; ++k) {
+    const int i = tid + k * kArThreads;
+    if (i < nvec) {
+      uint4 xv[VJ_TP_MAX_RANKS];
+#pragma unroll
+      for (int p = 0; p < VJ_TP_MAX_RANKS; ++p) {
+        const int row = p * S + j;
+        if (p < a.world && p != a.rank && row < a.rows) {
+          xv[p] = __ldcg(reinterpret_cast<const uint4 *>(a.results[p] + (size_t)row * H) + i);
+        }
+      }
+#pragma unroll
+      for (int p = 0; p < VJ_TP_MAX_RANKS; ++p) {
+        const int row = p * S + j;
+        if (p < a.world && p != a.rank && row < a.rows) {
+          reinterpret_cast<uint4 *>(a.residual_out + (size_t)row * H)[i] = xv[p];
+          const uint32_t o[4] = {xv[p].x, xv[p].y, xv[p].z, xv[p].w};
+          ss[p] += sq8(o);
+        }
+      }
+    }
+  }
+  block_sum_ranks(ss, red, a.world);
+#pragma unroll 1
+  for (int p = 0; p < a.world; ++p) {
+    const int row = p * S + j;
+    if (p == a.rank || row >= a.rows) continue;
+    const float ms = __fdiv_rn(static_cast<float>(ss[p]), static_cast<float>(H));
+    norm_row(a, row, __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps))));
+  }
+}
+
 __global__ void __launch_bounds__(kArThreads, kArCtasPerSm)
 allreduce_add_rmsnorm_kernel(ArArgs a) {
   const int b = blockIdx.x, G = gridDim.x, tid = threadIdx.x;
   __shared__ uint32_t s_epoch;
   __shared__ int s_fail;
-  __shared__ double red[kArThreads / 32];
+  __shared__ double red[(kArThreads / 32) * VJ_TP_MAX_RANKS];
   if (tid == 0) {
     s_epoch = a.epochs[b] + 1;
     a.epochs[b] = s_epoch;
@@ -237,12 +286,8 @@ allreduce_add_rmsnorm_kernel(ArArgs a) {
   // ... 2. every peer's slice is reduced (CTA b of rank p wrote exactly the
   // rows CTA b reads from it) ...
   if (!cta_barrier(a, 1, epoch, &s_fail)) return;
-  // ... 3. and gathers the other slices
-  for (int p = 0; p < a.world; ++p) {
-    if (p == a.rank) continue;
-    const int plo = p * S, phi = min(a.rows, plo + S);
-    for (int row = plo + b; row < phi; row += G) norm_row(a, row, gather_row(a, row, a.results[p], red));
-  }
+  // ... 3. and gathers the other slices (row j of every peer's slice at once)
+  for (int j = b; j < S; j += G) gather_rows(a, j, S, red);
 }
 
 }  // namespace
@@ -354,8 +399,16 @@ extern "C" vj_status vj_allreduce_add_rmsnorm(
   a.hidden = hidden;
   a.two_shot = results != nullptr && world > 1;
   a.eps = eps;
-  // every call launches the same grid, even with no rows: the per-CTA epochs
-  // and the peers' waits must advance together on all ranks
-  allreduce_add_rmsnorm_kernel<<<G, kArThreads, 0, stream>>>(a);
+  // Small batches take one barrier (one-shot) even with result buffers; the
+  // grid is one CTA per row a rank reduces, up to G. Every rank makes the
+  // same calls with the same rows, so CTA b's epoch advances in the same
+  // calls everywhere; a buffer is rewritten only after every peer has run a
+  // later call (stream order: its earlier kernel had finished), whatever the
+  // grid of that call.
+  a.gmax = G;
+  a.two_shot = a.two_shot && world > 2 && rows > kOneShotMaxRows;
+  const int64_t per_rank = a.two_shot ? (rows + world - 1) / world : rows;
+  const int grid = static_cast<int>(per_rank < 1 ? 1 : (per_rank < G ? per_rank : G));
+  allreduce_add_rmsnorm_kernel<<<grid, kArThreads, 0, stream>>>(a);
   return check_launch("vj_allreduce_add_rmsnorm");
 }
