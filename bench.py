@@ -1,25 +1,27 @@
 """Benchmark of the vllm-jax B200 hot path (one JSON line on rank 0).
 
-Default workload: paged decode attention at the Qwen3-8B
-head shape -- batch 256, one query token per sequence, context lengths
-log-uniform in [512, 32768] (seed 0), block_size 16, block tables drawn from a
-random permutation of a 200k-block pool, bf16 K/V ~ N(0, 1). Metric: paged-
-decode HBM GB/s (algorithmic bytes / time). One "step" = one decode-attention
-call over the whole batch (all KV heads of all sequences).
+Default workload (the first half of the headline metric):
+Qwen3-8B continuous batching through Engine.generate -- 512 requests, prompt
+and output lengths uniform in [100, 1024] (seed 0), random token ids, greedy,
+max_num_batched_tokens 16384, random-init N(0, 0.02) bf16 weights. Metric:
+output tokens/s of the whole job. One "step" = one generate() over the whole
+request set; --steps K times K of them (CUDA events, max over ranks) after
+--warmup W untimed ones.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|prefill|kvstore|e2e|c5] [--tp T]
+                    [--workload e2e|decode|prefill|kvstore|c5] [--tp T]
 
 N > 1 (torchrun, one process per GPU): tensor parallel by KV head -- rank r
-owns KV heads [r*8/N, (r+1)*8/N) of the same batch (its own pool slice); no
-collective on the data path. Total work is fixed, so scaling is "strong";
-`value` = algorithmic bytes of all ranks / max-over-ranks device time.
+holds KV heads [r*8/N, (r+1)*8/N), its q heads, 1/N of the MLP and its pool
+slice; o_proj and down_proj are summed over ranks by the fused NVLink
+all-reduce + residual add + RMSNorm kernel. Total work is fixed ("strong").
 
---workload prefill: C2 paged prefill attention (TFLOP/s). --workload kvstore:
-K3 (q/k norm + RoPE + KV scatter) on the C2 batch (GB/s). --workload e2e: C4,
-Qwen3-8B continuous batching through Engine.generate (output tok/s).
---workload c5: C5, Qwen3-32B with chunked prefill mixed with decode (output
-tok/s; --batch R runs the first R of the 1024 requests, and says so).
+--workload decode: C3 paged decode attention (HBM GB/s). --workload prefill:
+C2 paged prefill attention (TFLOP/s). --workload kvstore: K3 (q/k norm + RoPE
++ KV scatter) on the C2 batch (GB/s). --workload c5: C5, Qwen3-32B with
+chunked prefill mixed with decode (output tok/s; --batch R runs the first R
+of the 1024 requests, and says so). For the kernel workloads N > 1 splits the
+KV heads with no collective on the data path.
 
 --impl reference times the reference algorithm on the host CPU cores: the
 reference (JAX/Pallas) cannot be installed in this image, so its NumPy
@@ -74,6 +76,11 @@ def c2_batch(cfg=C2):
     S = cfg["num_seqs"]
     new = rng.integers(cfg["new_min"], cfg["new_max"] + 1, S).astype(np.int32)
     pre = rng.integers(cfg["prefix_min"], cfg["prefix_max"] + 1, S).astype(np.int32)
+    # profiling cases: every sequence the same length (--new-tokens / --prefix-tokens)
+    if cfg.get("new_fixed"):
+        new[:] = cfg["new_fixed"]
+    if cfg.get("prefix_fixed") is not None:
+        pre[:] = cfg["prefix_fixed"]
     ctx = new + pre
     bs = cfg["block_size"]
     perm = rng.permutation(cfg["pool_blocks"]).astype(np.int32)
@@ -1085,6 +1092,10 @@ def main():
                     help="profiling only: B sequences of the C3 / C2 batch (e2e: requests)")
     ap.add_argument("--pool-blocks", type=int, default=None,
                     help="profiling only: KV pool size in blocks (C3 / C2)")
+    ap.add_argument("--new-tokens", type=int, default=None,
+                    help="profiling only (prefill): every sequence this many new tokens")
+    ap.add_argument("--prefix-tokens", type=int, default=None,
+                    help="profiling only (prefill): every sequence this cached prefix")
     args = ap.parse_args()
     if args.batch is not None:
         C3["batch"] = args.batch
@@ -1092,6 +1103,10 @@ def main():
     if args.pool_blocks is not None:
         C3["pool_blocks"] = args.pool_blocks
         C2["pool_blocks"] = args.pool_blocks
+    if args.new_tokens is not None:
+        C2["new_fixed"] = args.new_tokens
+    if args.prefix_tokens is not None:
+        C2["prefix_fixed"] = args.prefix_tokens
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
