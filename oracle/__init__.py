@@ -30,12 +30,19 @@ Parity status:
   * host.py (scheduler, block manager, metadata) is PINNED: tests compare it
     with tests/golden/host_traces.json, recorded by importing the
     reference's own Python modules (tests/golden/make_golden.py).
-  * kv_store.py / attention.py / qwen3.py / sampler.py: the reference's
-    JAX/XLA numerics cannot run in this image (no jax, no flax), and no
-    reference test pins them, so they are "parity unpinned": the restatement
-    follows the reference's code and documented semantics (fp32 logits and
-    softmax, bf16 rounding after every jnp op of apply_rope, flax RMSNorm
-    statistics in fp32). XLA's fusion may keep excess fp32 precision between
-    ops, which can move single bf16 ulps; JAX's threefry sampling stream is
-    not reproduced, so draws are checked in distribution.
+  * kv_store.py (RoPE, KV-slot scatter) and attention.py are PINNED:
+    tests/test_numeric_golden.py compares them with tests/golden/numerics.npz,
+    produced by running the reference's own apply_rope, _update_kv_cache,
+    attention() (default Pallas path and jnp path) and its two *_reference
+    functions under a numpy + ml_dtypes JAX stand-in
+    (tests/golden/make_numeric_golden.py, tests/golden/jax_shim.py):
+    RoPE and slot writes bit for bit, attention within max-abs 2e-2 /
+    mean-abs 2e-3. The stand-in rounds after every op; XLA may fuse ops and
+    keep f32 between them, which can move single bf16 ulps.
+  * RMSNorm comes from flax (not in the reference tree): restated as fp32
+    statistics, bf16(x * (rsqrt(mean(x^2) + eps) * scale)), the 128-dim q/k
+    rows summed in the fixed fp32 order of vj_kv_store_qknorm_rope.
+  * qwen3.py composes the pinned pieces with the reference's layer dataflow;
+    sampler.py checks kept sets exactly and draws in distribution (JAX's
+    threefry stream is not reproduced).
 """
