@@ -230,6 +230,43 @@ VJ_API vj_status vj_paged_prefill(
     int32_t *error_flag, cudaStream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * K1 + K2 in one launch for a chunked-prefill step that mixes decode rows
+ * with prompt chunks (the reference schedules prefill and decode as separate
+ * batches, vllm/src/scheduler.py:27-63, and has no such step; this replaces
+ * the two attention calls such a step would make with one).
+ *
+ *   sequences [0, num_decode) are decode rows: q row b holds sequence b's one
+ *   new token; sequences [num_decode, num_seqs) are prompt chunks after a
+ *   cached prefix, rows [cu_seqlens_q[s], cu_seqlens_q[s+1]) as in
+ *   vj_paged_prefill (cu_seqlens_q[s] == s for the decode rows); rows past
+ *   cu_seqlens_q[num_seqs] (padding) are written as 0
+ *   block_tables [num_seqs, bt_width], context_lens [num_seqs] (keys already
+ *   in the pool, the new tokens included) for both kinds
+ *   scale: applied to q.k in fp32 for both kinds
+ *   workspace: decode split-KV scratch of
+ *   vj_paged_attention_mixed_workspace_size(num_decode, Hq, D, max_chunks)
+ *   bytes; plan = 0 reuses the split plan of an earlier call on the same
+ *   stream with the same decode rows (the later layers of a step), as
+ *   vj_paged_decode_planned does
+ * Launches: the decode plan (plan != 0, decode rows present), one kernel
+ * whose first CTAs run the split-KV decode warps, the next ones prefill tile
+ * pairs and the last few zero the padding rows, and the decode combine.
+ * error_flag as vj_paged_prefill.
+ * ------------------------------------------------------------------------- */
+VJ_API size_t vj_paged_attention_mixed_workspace_size(int32_t num_decode, int32_t num_q_heads,
+                                                      int32_t head_dim, int32_t max_chunks);
+
+VJ_API vj_status vj_paged_attention_mixed(
+    const void *q, const void *k_cache, const void *v_cache,
+    const int32_t *block_tables, const int32_t *cu_seqlens_q,
+    const int32_t *context_lens, void *out, int64_t num_tokens, int32_t num_seqs,
+    int32_t num_decode, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+    int64_t num_blocks, int32_t block_size, int32_t bt_width, int32_t bt_stride,
+    int64_t stride_block, int64_t stride_token, int64_t stride_head, int32_t max_seqlen_q,
+    float scale, int32_t max_chunks, int32_t plan, void *workspace, size_t workspace_bytes,
+    int32_t *error_flag, cudaStream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Fused decoder-layer epilogues (vllm/model/qwen3.py:375-389, :337-341).
  * vj_add_rmsnorm: r = bf16(x + residual) (stored to residual_out when given;
  * residual may be NULL for a plain norm), y = bf16(r * (rsqrt(mean(r^2) +

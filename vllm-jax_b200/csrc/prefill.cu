@@ -36,7 +36,16 @@
 #include "../../include/vjattn.h"
 #include "vj_common.cuh"
 
+#include <algorithm>
 #include <string>
+
+namespace vj {
+namespace {
+namespace dk {
+#include "decode_core.cuh"
+}  // namespace dk
+}  // namespace
+}  // namespace vj
 
 namespace vj {
 namespace {
@@ -149,12 +158,11 @@ VJ_DEV bool produce_kv(const CUtensorMap *tm, uint8_t *ring, uint64_t *full, uin
   return true;
 }
 
-// 11 warps: a sub-partition holds 3 of them in its 16K registers -> <= 168 each.
-__global__ void __launch_bounds__(kThreads, 1)
-prefill_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-               const __grid_constant__ CUtensorMap tmv, PrefillArgs a) {
-  const int s = blockIdx.z, h = blockIdx.y;
-  const int m2 = gridDim.x - 1 - blockIdx.x;  // longest tile pairs first
+// The work of one CTA: tile pair m2 of (sequence s, kv head h). All 352
+// threads of the CTA run it.
+__device__ __forceinline__ void prefill_body(const CUtensorMap *tmq_p, const CUtensorMap *tmk_p,
+                                             const CUtensorMap *tmv_p, const PrefillArgs &a,
+                                             int s, int h, int m2, uint8_t *smem_raw) {
   const int q0 = __ldg(a.cu + s);
   const int n = __ldg(a.cu + s + 1) - q0;
   const int tq0 = m2 * 2 * a.tt;               // first token of tile A
@@ -165,7 +173,6 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
   const int kv_end = p0 + min(n, tq0 + 2 * a.tt);  // keys visible to the last row of B
   const int nkv = (kv_end + kBN - 1) / kBN;
 
-  extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
   Bars &bar = *reinterpret_cast<Bars *>(smem + OFF_BAR);
@@ -192,18 +199,18 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
   if (warp == kWarpK) {
     // ------------------------------------------------------------ Q + K producer
     if (lane == 0) {
-      tma_prefetch_desc(&tmq); tma_prefetch_desc(&tmk); tma_prefetch_desc(&tmv);
+      tma_prefetch_desc(tmq_p); tma_prefetch_desc(tmk_p); tma_prefetch_desc(tmv_p);
       mbar_arrive_expect_tx(&bar.q_full, 2 * kTile);
       for (int t = 0; t < 2; ++t) {
         const int tok = q0 + tq0 + t * a.tt;
-        tma_load_3d(smem + OFF_Q + t * kTile, &tmq, &bar.q_full, 0, h * a.g, tok);
-        tma_load_3d(smem + OFF_Q + t * kTile + kHalf, &tmq, &bar.q_full, 64, h * a.g, tok);
+        tma_load_3d(smem + OFF_Q + t * kTile, tmq_p, &bar.q_full, 0, h * a.g, tok);
+        tma_load_3d(smem + OFF_Q + t * kTile + kHalf, tmq_p, &bar.q_full, 64, h * a.g, tok);
       }
     }
-    ok = produce_kv<kKStages>(&tmk, smem + OFF_K, bar.k_full, bar.k_empty, a, s, h, nkv, lane);
+    ok = produce_kv<kKStages>(tmk_p, smem + OFF_K, bar.k_full, bar.k_empty, a, s, h, nkv, lane);
   } else if (warp == kWarpV) {
     // ------------------------------------------------------------ V producer
-    ok = produce_kv<kVStages>(&tmv, smem + OFF_V, bar.v_full, bar.v_empty, a, s, h, nkv, lane);
+    ok = produce_kv<kVStages>(tmv_p, smem + OFF_V, bar.v_full, bar.v_empty, a, s, h, nkv, lane);
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -381,6 +388,61 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
   if (warp == kWarpMma) tmem_dealloc(tmem, 512);
 }
 
+// 11 warps: a sub-partition holds 3 of them in its 16K registers -> <= 168 each.
+__global__ void __launch_bounds__(kThreads, 1)
+prefill_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+               const __grid_constant__ CUtensorMap tmv, PrefillArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  // longest tile pairs first
+  prefill_body(&tmq, &tmk, &tmv, a, blockIdx.z, blockIdx.y, gridDim.x - 1 - blockIdx.x,
+               smem_raw);
+}
+
+// Mixed step (chunked prefill): one launch runs the decode rows and the
+// prompt chunks. CTAs [0, n_dec) are decode CTAs: kMixedDecodeWarps warps
+// each run the split-KV decode warp loop (work items pulled from the
+// workspace's queue, as in decode_chunk_kernel); the other warps leave. The
+// remaining CTAs are prefill tile pairs, numbered pair-fastest, then kv head,
+// then sequence (the 3-D grid of prefill_kernel, flattened). One CTA fits an
+// SM (shared memory), so decode CTAs stream K/V on their SMs while prefill
+// CTAs keep the tensor cores busy on the others.
+constexpr int kMixedDecodeWarps = 8;
+static_assert(dk::smem_bytes(kMixedDecodeWarps) <= kSmemBytes, "decode CTAs fit the smem");
+
+__global__ void __launch_bounds__(kThreads, 1)
+attention_mixed_kernel(const __grid_constant__ CUtensorMap tmq,
+                       const __grid_constant__ CUtensorMap tmk,
+                       const __grid_constant__ CUtensorMap tmv, PrefillArgs pa,
+                       dk::DecodeArgs da, int n_dec, int mpairs, int n_pre_ctas,
+                       int num_seqs) {
+  extern __shared__ uint8_t smem_raw[];
+  if (static_cast<int>(blockIdx.x) >= n_dec + n_pre_ctas) {
+    // rows past cu_seqlens_q[num_seqs] (padding) -> 0
+    const int64_t row_elems = (int64_t)pa.Hq * kD;
+    const int64_t start = (int64_t)__ldg(pa.cu - da.B + num_seqs) * row_elems;
+    const int64_t end = (int64_t)pa.num_tokens * row_elems;
+    const int64_t tail = static_cast<int>(blockIdx.x) - n_dec - n_pre_ctas;
+    const int64_t n_tail = gridDim.x - n_dec - n_pre_ctas;
+    uint4 *o = reinterpret_cast<uint4 *>(pa.out);
+    for (int64_t i = start / 8 + tail * blockDim.x + threadIdx.x; i < end / 8;
+         i += n_tail * blockDim.x) {
+      o[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    return;
+  }
+  if (static_cast<int>(blockIdx.x) < n_dec) {
+    const int warp = threadIdx.x >> 5;
+    if (warp >= kMixedDecodeWarps) return;   // decode CTAs use no block-wide barrier
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    dk::decode_chunk_body<kMixedDecodeWarps>(&tmk, &tmv, da, smem, warp, threadIdx.x & 31);
+    return;
+  }
+  const int idx = static_cast<int>(blockIdx.x) - n_dec;
+  const int x = idx % mpairs, rest = idx / mpairs;
+  prefill_body(&tmq, &tmk, &tmv, pa, rest / pa.Hkv, rest % pa.Hkv, mpairs - 1 - x, smem_raw);
+}
+
 // Rows of the packed output past cu_seqlens_q[num_seqs] (bucket padding) -> 0,
 // as the reference's scatter leaves them (prefill_paged_attention.py:384-388).
 __global__ void prefill_zero_tail_kernel(__nv_bfloat16 *out, const int32_t *cu, int num_seqs,
@@ -485,4 +547,148 @@ extern "C" vj_status vj_paged_prefill(
   prefill_zero_tail_kernel<<<num_sms() * 2, 256, 0, stream>>>(
       static_cast<__nv_bfloat16 *>(out), cu_seqlens_q, num_seqs, num_tokens, num_q_heads * kD);
   return check_launch("vj_paged_prefill(zero tail)");
+}
+
+extern "C" size_t vj_paged_attention_mixed_workspace_size(int32_t num_decode,
+                                                          int32_t num_q_heads, int32_t head_dim,
+                                                          int32_t max_chunks) {
+  if (num_decode < 0 || num_q_heads <= 0 || head_dim != vj::kD) return 0;
+  if (max_chunks <= 0) max_chunks = 4096 + num_decode;
+  return vj::dk::workspace_bytes(num_decode, num_q_heads, max_chunks);
+}
+
+extern "C" vj_status vj_paged_attention_mixed(
+    const void *q, const void *k_cache, const void *v_cache, const int32_t *block_tables,
+    const int32_t *cu_seqlens_q, const int32_t *context_lens, void *out, int64_t num_tokens,
+    int32_t num_seqs, int32_t num_decode, int32_t num_q_heads, int32_t num_kv_heads,
+    int32_t head_dim, int64_t num_blocks, int32_t block_size, int32_t bt_width,
+    int32_t bt_stride, int64_t stride_block, int64_t stride_token, int64_t stride_head,
+    int32_t max_seqlen_q, float scale, int32_t max_chunks, int32_t plan, void *workspace,
+    size_t workspace_bytes, int32_t *error_flag, cudaStream_t stream) {
+  using namespace vj;
+  if (num_tokens < 0 || num_seqs < 0 || num_decode < 0 || num_decode > num_seqs ||
+      num_q_heads <= 0 || num_kv_heads <= 0 || num_blocks <= 0 || bt_width < 0 ||
+      bt_stride < bt_width) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_paged_attention_mixed: bad sizes");
+  }
+  if (num_q_heads % num_kv_heads != 0) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT,
+                     "vj_paged_attention_mixed: Number of Q heads must be divisible by number "
+                     "of KV heads");
+  }
+  const int g = num_q_heads / num_kv_heads;
+  if (head_dim != kD) {
+    return set_error(VJ_ERR_UNSUPPORTED, "vj_paged_attention_mixed: head_dim must be 128");
+  }
+  if (g > 8 || kBM % g != 0 || num_kv_heads > 255) {
+    return set_error(VJ_ERR_UNSUPPORTED,
+                     "vj_paged_attention_mixed: query heads per KV head must be <= 8 and divide "
+                     "128; at most 255 KV heads");
+  }
+  if (block_size <= 0 || block_size % kPageTok != 0 ||
+      stride_block != (int64_t)block_size * stride_token) {
+    return set_error(VJ_ERR_UNSUPPORTED,
+                     "vj_paged_attention_mixed: block_size must be a multiple of 16 with evenly "
+                     "strided tokens");
+  }
+  if (num_blocks * block_size > (int64_t)INT32_MAX || num_tokens > (int64_t)INT32_MAX) {
+    return set_error(VJ_ERR_UNSUPPORTED, "vj_paged_attention_mixed: sizes beyond 2^31");
+  }
+  if (num_tokens == 0 || num_seqs == 0) return VJ_OK;
+  if (!q || !k_cache || !v_cache || !block_tables || !cu_seqlens_q || !context_lens || !out ||
+      !error_flag) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_paged_attention_mixed: null pointer");
+  }
+  if (max_chunks <= 0) max_chunks = 4096 + num_decode;
+  if (num_decode > 0) {
+    if (max_chunks <= num_decode || max_chunks >= (1 << 23)) {
+      return set_error(VJ_ERR_INVALID_ARGUMENT,
+                       "vj_paged_attention_mixed: max_chunks must exceed num_decode, below 2^23");
+    }
+    const size_t need = dk::workspace_bytes(num_decode, num_q_heads, max_chunks);
+    if (!workspace || workspace_bytes < need ||
+        reinterpret_cast<uintptr_t>(workspace) % 16 != 0) {
+      return set_error(VJ_ERR_WORKSPACE, "vj_paged_attention_mixed: workspace needs " +
+                                             std::to_string(need) + " bytes, 16-byte aligned");
+    }
+  }
+  const int tt = kBM / g;
+  CUtensorMap tmq, tmk, tmv;
+  int rc = encode_tmap_3d(&tmq, q, kD, num_q_heads, num_tokens, (uint64_t)kD * 2,
+                          (uint64_t)num_q_heads * kD * 2, 64, g, tt, true);
+  if (rc) return rc;
+  const uint64_t ntok = (uint64_t)num_blocks * block_size;
+  const bool head_major = stride_head < stride_token;
+  for (int i = 0; i < 2; ++i) {
+    CUtensorMap *mp = i ? &tmv : &tmk;
+    const void *base = i ? v_cache : k_cache;
+    rc = head_major ? encode_tmap_3d(mp, base, kD, num_kv_heads, ntok, stride_head * 2,
+                                     stride_token * 2, 64, 1, kPageTok, true)
+                    : encode_tmap_3d(mp, base, kD, ntok, num_kv_heads, stride_token * 2,
+                                     stride_head * 2, 64, kPageTok, 1, true);
+    if (rc) return rc;
+  }
+  // prompt chunks: sequences [num_decode, num_seqs)
+  const int n_pre = num_seqs - num_decode;
+  PrefillArgs pa;
+  pa.out = static_cast<__nv_bfloat16 *>(out);
+  pa.bt = block_tables + (size_t)num_decode * bt_stride;
+  pa.cu = cu_seqlens_q + num_decode;
+  pa.ctx_lens = context_lens + num_decode;
+  pa.Hq = num_q_heads; pa.Hkv = num_kv_heads; pa.g = g; pa.tt = tt;
+  pa.bt_stride = bt_stride;
+  pa.pages_per_block = block_size / kPageTok;
+  pa.max_pages = bt_width * pa.pages_per_block;
+  pa.block_size = block_size;
+  pa.num_blocks = (int)num_blocks;
+  pa.head_major = head_major ? 1 : 0;
+  pa.num_tokens = (int)num_tokens;
+  pa.scale_log2 = scale * kLog2e;
+  pa.err = error_flag;
+  // decode rows: sequences [0, num_decode), q row b = sequence b
+  dk::DecodeArgs da{};
+  da.q = static_cast<const __nv_bfloat16 *>(q);
+  da.out = static_cast<__nv_bfloat16 *>(out);
+  da.bt = block_tables;
+  da.lens = context_lens;
+  da.B = num_decode; da.Hq = num_q_heads; da.Hkv = num_kv_heads; da.g = g;
+  da.bt_stride = bt_stride;
+  da.pages_per_block = block_size / kPageTok;
+  da.max_pages = bt_width * da.pages_per_block;
+  da.block_size = block_size;
+  da.num_blocks = (int)num_blocks;
+  da.head_major = head_major ? 1 : 0;
+  da.scale_log2 = scale * kLog2e;
+  // decode CTAs: half the SMs when prompt chunks share the launch, else all
+  const int n_dec = num_decode == 0 ? 0 : (n_pre > 0 ? std::max(1, num_sms() / 2) : num_sms());
+  if (num_decode > 0) {
+    da.ws = dk::carve(workspace, num_decode, num_q_heads, max_chunks);
+    if (plan) {
+      dk::decode_plan_kernel<<<1, 1024, 0, stream>>>(context_lens, num_decode, num_kv_heads,
+                                                     max_chunks, n_dec * kMixedDecodeWarps,
+                                                     da.max_pages, da.ws);
+      rc = check_launch("vj_paged_attention_mixed(plan)");
+      if (rc) return rc;
+    }
+  }
+  const int64_t maxq = max_seqlen_q > 0 ? max_seqlen_q : num_tokens;
+  const int64_t mpairs = n_pre > 0 ? std::max<int64_t>(1, (maxq + 2 * tt - 1) / (2 * tt)) : 1;
+  const int64_t n_pre_ctas = n_pre > 0 ? mpairs * num_kv_heads * n_pre : 0;
+  constexpr int kTailCtas = 8;   // zero the rows past cu_seqlens_q[num_seqs]
+  const int64_t grid = n_dec + n_pre_ctas + kTailCtas;
+  if (grid > INT32_MAX) {
+    return set_error(VJ_ERR_UNSUPPORTED, "vj_paged_attention_mixed: grid too large");
+  }
+  cudaFuncSetAttribute(attention_mixed_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)kSmemBytes);
+  attention_mixed_kernel<<<(unsigned)grid, kThreads, kSmemBytes, stream>>>(
+      tmq, tmk, tmv, pa, da, n_dec, (int)mpairs, (int)n_pre_ctas, num_seqs);
+  rc = check_launch("vj_paged_attention_mixed");
+  if (rc) return rc;
+  if (num_decode > 0) {
+    const int warps = num_decode * num_q_heads;
+    dk::decode_combine_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(da);
+    rc = check_launch("vj_paged_attention_mixed(combine)");
+  }
+  return rc;
 }

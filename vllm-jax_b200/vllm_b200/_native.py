@@ -58,6 +58,14 @@ PROTOTYPES: dict[str, tuple] = {
         c_i64, c_i32, c_i32, c_i32,                 # nb, bs, bt_width, bt_stride
         c_i64, c_i64, c_i64,                        # strides
         c_i32, c_f32, c_vp, c_vp]),                 # max_seqlen_q, scale, err, stream
+    "vj_paged_attention_mixed_workspace_size": (c_sz, [c_i32, c_i32, c_i32, c_i32]),
+    "vj_paged_attention_mixed": (c_int, [
+        c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,   # q, k, v, bt, cu_q, ctx_lens, out
+        c_i64, c_i32, c_i32, c_i32, c_i32, c_i32,   # T, S, num_decode, Hq, Hkv, D
+        c_i64, c_i32, c_i32, c_i32,                 # nb, bs, bt_width, bt_stride
+        c_i64, c_i64, c_i64,                        # strides
+        c_i32, c_f32, c_i32, c_i32,                 # max_seqlen_q, scale, max_chunks, plan
+        c_vp, c_sz, c_vp, c_vp]),                   # ws, ws_bytes, err, stream
     "vj_build_metadata": (c_int, [
         c_i32, c_vp, c_vp, c_vp, c_i32,             # mode, slots, starts, lens, num_seqs
         c_vp, c_i32, c_vp, c_vp, c_i32,             # token_table, stride, block_pool, nblocks, bt_stride
@@ -131,7 +139,8 @@ def check(status: int) -> None:
 
 # kernels launched by one successful call of each entry point
 KERNELS_PER_CALL = {"vj_paged_decode": 3, "vj_paged_decode_planned": 2,
-                    "vj_paged_decode_noalloc": 3, "vj_paged_prefill": 2}
+                    "vj_paged_decode_noalloc": 3, "vj_paged_prefill": 2,
+                    "vj_paged_attention_mixed": 3}
 launch_count = 0
 
 

@@ -131,3 +131,53 @@ def paged_prefill(q: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.T
     strides = (k.stride(0), k.stride(1), k.stride(2))
     return _launch(q, k, v, nb, bs, strides, hkv, block_tables, cu_seqlens_q, context_lens,
                    max_seqlen_q, scale, out)
+
+
+def paged_attention_mixed(q: torch.Tensor, kv_cache: torch.Tensor, block_tables: torch.Tensor,
+                          cu_seqlens_q: torch.Tensor, context_lens: torch.Tensor,
+                          num_decode: int, max_seqlen_q: int, scale: float | None = None,
+                          out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                          reuse_plan: bool = False, max_chunks: int = 0) -> torch.Tensor:
+    """Attention of a chunked-prefill step in ONE kernel launch (plus the
+    decode plan and combine): sequences [0, num_decode) are decode rows (q row
+    b = sequence b), the rest prompt chunks after a cached prefix; rows past
+    cu_seqlens_q[-1] (padding) come out 0. Keys of the new tokens must already
+    be in the cache. reuse_plan: keep the decode split
+    plan of the previous call on this stream (same decode rows)."""
+    from ._util import workspace as scratch
+    require_dtype(q, torch.bfloat16, "q")
+    require_dtype(kv_cache, torch.bfloat16, "kv_cache")
+    for name, t in (("block_tables", block_tables), ("cu_seqlens_q", cu_seqlens_q),
+                    ("context_lens", context_lens)):
+        require_dtype(t, torch.int32, name)
+    S = cu_seqlens_q.shape[0] - 1
+    if block_tables.shape[0] != S or context_lens.shape != (S,):
+        raise ValueError("block_tables and context_lens need one row per sequence")
+    if not 0 <= num_decode <= S:
+        raise ValueError("num_decode must lie in [0, num_seqs]")
+    if kv_cache.dim() != 5 or kv_cache.shape[0] != 2:
+        raise ValueError("kv_cache must have shape (2, num_blocks, block_size, Hkv, D)")
+    if not q.is_contiguous() or block_tables.stride(-1) != 1:
+        raise ValueError("q and block_tables must be contiguous")
+    dev = require_cuda(q, kv_cache, block_tables, cu_seqlens_q, context_lens)
+    T, Hq, D = q.shape
+    k, v = kv_cache[0], kv_cache[1]
+    nb, bs, hkv, _ = k.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty_like(q)
+    ws_bytes = _native.load().vj_paged_attention_mixed_workspace_size(num_decode, Hq, D,
+                                                                      max_chunks)
+    if workspace is None:
+        workspace = scratch(dev, max(ws_bytes, 16), "decode")
+    elif workspace.dtype != torch.uint8 or workspace.numel() < ws_bytes:
+        raise ValueError(f"decode workspace must be uint8 with >= {ws_bytes} bytes")
+    _native.call("vj_paged_attention_mixed", q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                 block_tables.data_ptr(), cu_seqlens_q.data_ptr(), context_lens.data_ptr(),
+                 out.data_ptr(), T, S, int(num_decode), Hq, hkv, D, nb, bs,
+                 block_tables.shape[1], block_tables.stride(0), k.stride(0), k.stride(1),
+                 k.stride(2), int(max_seqlen_q), float(scale), int(max_chunks),
+                 0 if reuse_plan else 1, workspace.data_ptr(), workspace.numel(),
+                 _err_flag(dev).data_ptr(), stream_ptr(dev))
+    return out

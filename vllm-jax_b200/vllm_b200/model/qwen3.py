@@ -29,7 +29,7 @@ import torch.nn.functional as F
 from ..kernels.decode_paged_attention import paged_decode
 from ..kernels.fused import add_rmsnorm, silu_mul
 from ..kernels.kv_store import kv_store_qknorm_rope
-from ..kernels.prefill_paged_attention import paged_prefill
+from ..kernels.prefill_paged_attention import paged_attention_mixed, paged_prefill
 
 
 @dataclass
@@ -316,25 +316,22 @@ class Qwen3Model:
     def forward_mixed(self, meta, kv_caches: list[torch.Tensor], num_decode: int,
                       sample_rows: torch.Tensor) -> torch.Tensor:
         """Chunked-prefill step over meta (ranges metadata): sequences
-        [0, num_decode) contribute one token each and go through the decode
-        kernel; the rest are prompt chunks after a cached prefix (prefill
-        kernel with context_lens). Returns bf16 logits of `sample_rows`."""
+        [0, num_decode) contribute one token each, the rest are prompt chunks
+        after a cached prefix; each layer's attention over both kinds is ONE
+        kernel launch (vj_paged_attention_mixed: split-KV decode CTAs next to
+        tcgen05 prefill CTAs), whose decode split plan the later layers reuse.
+        Returns bf16 logits of `sample_rows`."""
         x = self.embed(meta.input_ids)
         S, nd = meta.num_seqs, num_decode
 
         planned = []
 
         def attn(q, kv):
-            out = torch.empty_like(q)
-            if nd:
-                paged_decode(q[:nd], kv, meta.block_tables[:nd], meta.context_lens[:nd],
-                             self.scale, out=out[:nd], workspace=self.decode_workspace,
-                             reuse_plan=bool(planned) and self.decode_workspace is not None)
-                planned.append(True)
-            if S > nd:
-                paged_prefill(q, kv, meta.block_tables[nd:S], meta.cu_seqlens_q[nd:S + 1],
-                              meta.context_lens[nd:S], max_seqlen_q=meta.max_new,
-                              scale=self.scale, out=out)
+            out = paged_attention_mixed(
+                q, kv, meta.block_tables[:S], meta.cu_seqlens_q[:S + 1], meta.context_lens[:S],
+                nd, meta.max_new, self.scale, workspace=self.decode_workspace,
+                reuse_plan=bool(planned) and nd > 0 and self.decode_workspace is not None)
+            planned.append(True)
             return out
 
         x = self._stack(x, kv_caches, meta, attn)
