@@ -23,8 +23,8 @@
 // Warp roles (352 threads):
 //   warps 0-3 / 4-7  softmax of tile A / B: one thread per row; per key tile
 //                    read S (128 fp32 columns) from TMEM, online softmax in
-//                    fp32 with exp2 (a fixed share on an FMA polynomial to
-//                    offload the MUFU unit), P back to TMEM; O is rescaled
+//                    fp32 with exp2 (row max with three-input max.f32, scale
+//                    and sums on packed f32x2 ops), P back to TMEM; O is rescaled
 //                    in TMEM only when the running max grows by more than
 //                    2^8 (exact: l and O always share the same reference max)
 //   warp 8           TMA producer of K tiles (and Q once)
@@ -68,17 +68,25 @@ constexpr uint32_t TM_S = 0, TM_O = 256;        // + tile * 128
 constexpr float kRescaleThreshold = 8.0f;       // log2 units
 constexpr float kLog2e = 1.4426950408889634f;
 
-// Softmax exponentials are split between the MUFU unit (ex2.approx) and a
-// cubic polynomial on the FMA pipe: with two Q tiles per key tile, MUFU work
-// equals the tensor-core time. Bit k of kEmuMask set -> columns i with
-// i % 8 == k use the polynomial. 2^f on [-0.5, 0.5] is approximated by a
-// cubic fitted for minimum relative error (max 2.1e-4, well below bf16's 2^-9
-// rounding of P).
+// Softmax exponentials run on the MUFU unit (ex2.approx). Bit k of kEmuMask
+// set moves the columns i with i % 8 == k onto a cubic polynomial on the FMA
+// pipe instead (2^f on [-0.5, 0.5], fitted for minimum relative error, max
+// 2.1e-4, below bf16's 2^-9 rounding of P). Measured on C2 with the packed
+// fp32 softmax arithmetic: 990 TFLOP/s with no column on the polynomial, 939
+// with 1 of 8, 849 and 722 with 2 and 4 of 8 (before packing): the softmax
+// threads are bound by issue, not by MUFU, so the default moves none.
 #ifndef VJ_PREFILL_EMU_MASK
-#define VJ_PREFILL_EMU_MASK 0x80
+#define VJ_PREFILL_EMU_MASK 0x00
 #endif
 constexpr unsigned kEmuMask = VJ_PREFILL_EMU_MASK;
 constexpr float kP0 = 0.99995905f, kP1 = 0.69357258f, kP2 = 0.24221395f, kP3 = 0.05302752f;
+
+// max of three (sm_100 three-input max.f32; exact, like two fmaxf)
+VJ_DEV float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 
 VJ_DEV float poly_exp2(float x) {
   x = fmaxf(x, -125.f);                  // keeps the exponent field positive
@@ -300,10 +308,12 @@ __device__ __forceinline__ void prefill_body(const CUtensorMap *tmq_p, const CUt
 #pragma unroll
       for (int k = 0; k < 8; ++k) mx8[k] = sv[k];
 #pragma unroll
-      for (int i = 8; i < kBN; i += 8) {
+      for (int i = 8; i < kBN - 8; i += 16) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], sv[i + k]);
+        for (int k = 0; k < 8; ++k) mx8[k] = fmax3(mx8[k], sv[i + k], sv[i + 8 + k]);
       }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], sv[kBN - 8 + k]);
       const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                              fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       // scores are raw q.k; the softmax scale (and log2 e) folds into one FFMA
@@ -313,25 +323,31 @@ __device__ __forceinline__ void prefill_body(const CUtensorMap *tmq_p, const CUt
       const float corr = j == 0 ? 0.f : fast_exp2(m_run - m_use);
       // exponentials, row sum and P (bf16 pairs) in two 64-key halves so P
       // of the first half is in TMEM before the second half is computed
-      float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // (scale and max subtraction, and the 8 running sums, on packed fp32
+      // pairs: the same roundings as the scalar FFMA / FADD, half the issue)
+      uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
+      const uint64_t sc2 = f32x2(a.scale_log2, a.scale_log2), nm2 = f32x2(-m_use, -m_use);
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         uint32_t pw[32];
 #pragma unroll
         for (int i = 0; i < kBN / 2; i += 8) {
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const float x = fmaf(sv[hf * 64 + i + k], a.scale_log2, -m_use);
-            sv[hf * 64 + i + k] = ((kEmuMask >> k) & 1u) ? poly_exp2(x) : fast_exp2(x);
-            sum8[k] += sv[hf * 64 + i + k];
-          }
-#pragma unroll
           for (int k = 0; k < 8; k += 2) {
-            pw[(i + k) / 2] = pack_bf16(sv[hf * 64 + i + k], sv[hf * 64 + i + k + 1]);
+            float x0, x1;
+            f32x2_split(f32x2_fma(f32x2(sv[hf * 64 + i + k], sv[hf * 64 + i + k + 1]), sc2, nm2),
+                        x0, x1);
+            const float e0 = ((kEmuMask >> k) & 1u) ? poly_exp2(x0) : fast_exp2(x0);
+            const float e1 = ((kEmuMask >> (k + 1)) & 1u) ? poly_exp2(x1) : fast_exp2(x1);
+            sum2[k / 2] = f32x2_add(sum2[k / 2], f32x2(e0, e1));
+            pw[(i + k) / 2] = pack_bf16(e0, e1);
           }
         }
         tmem_st32u_nowait(tS + hf * 32, pw);
       }
+      float sum8[8];
+#pragma unroll
+      for (int k = 0; k < 8; k += 2) f32x2_split(sum2[k / 2], sum8[k], sum8[k + 1]);
       const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) +
                         ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       l_run = l_run * corr + sum;
