@@ -18,7 +18,8 @@ all-reduce + residual add + RMSNorm kernel. Total work is fixed ("strong").
 
 --workload decode: C3 paged decode attention (HBM GB/s). --workload prefill:
 C2 paged prefill attention (TFLOP/s). --workload kvstore: K3 (q/k norm + RoPE
-+ KV scatter) on the C2 batch (GB/s). --workload c5: C5, Qwen3-32B with
++ KV scatter) on the C2 batch (GB/s). --workload c4step: one Qwen3-8B decode
+step as a CUDA graph (ms) with per-kernel shares on stderr. --workload c5: C5, Qwen3-32B with
 chunked prefill mixed with decode (output tok/s; --batch R runs the first R
 of the 1024 requests, and says so). For the kernel workloads N > 1 splits the
 KV heads with no collective on the data path.
@@ -1069,13 +1070,111 @@ def run_e2e(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def run_c4step(args, rank, world, local_rank):
+    """One Qwen3-8B decode step (the C4 engine's decode forward: 36 layers,
+    K3, paged decode, cuBLAS GEMMs, norms, lm_head) replayed as a CUDA graph
+    at batch --batch (default 512) and context --context (default 840, C4's
+    mean context during generation), device-timed with CUDA events; the
+    per-kernel shares of three replays (torch profiler) go to stderr. Its
+    roofline: weights + KV of every context token per step."""
+    import collections
+
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    from vllm_b200 import _native
+    from vllm_b200.kernels.decode_paged_attention import decode_workspace_bytes
+    from vllm_b200.kernels.kv_store import rope_table
+    from vllm_b200.kernels.metadata import DecodeMeta
+    from vllm_b200.model.qwen3 import Qwen3Model, Qwen3Weights, get_config
+    if world > 1:
+        raise SystemExit("--workload c4step runs on one GPU")
+    B, L = args.batch or 512, args.context
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    cfg = get_config("Qwen3-8B")
+    w = Qwen3Weights(cfg, dev, seed=0)
+    m = Qwen3Model(w)
+    bs, D, Hkv = 16, cfg.head_dim, cfg.num_key_value_heads
+    pages = (L + bs - 1) // bs
+    nb = B * pages + 8
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5)
+    kv = [torch.randn((2, nb, bs, Hkv, D), generator=gen, device=dev).to(torch.bfloat16)
+          for _ in range(cfg.num_hidden_layers)]
+    m.decode_workspace = torch.empty(decode_workspace_bytes(B, cfg.num_attention_heads, D),
+                                     dtype=torch.uint8, device=dev)
+    m.rope_table = rope_table(dev, cfg.rope_theta, L + 1)
+    perm = torch.randperm(B * pages, generator=gen, device=dev).to(torch.int32)
+    bt = perm.view(B, pages)
+    ctx = torch.full((B,), L, device=dev, dtype=torch.int32)
+    ids = torch.randint(0, cfg.vocab_size, (B,), generator=gen, device=dev).to(torch.int32)
+    slots = (bt[:, -1] * bs + (L - 1) % bs).to(torch.int32)
+    meta = DecodeMeta(ids, ctx - 1, slots, bt, ctx, B)
+    for _ in range(max(args.warmup, 3)):
+        m.forward_decode(meta, kv)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    before = _native.launch_count
+    with torch.cuda.graph(graph):
+        m.forward_decode(meta, kv)
+    per_step = _native.launch_count - before
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    wbytes = sum(p.numel() * 2 for lw in w.layers for p in
+                 (lw.w_qkv, lw.w_o, lw.w_gate_up, lw.w_down)) + w.lm_head.numel() * 2
+    kvbytes = B * L * cfg.num_hidden_layers * 2 * Hkv * D * 2
+    peaks, src = load_peaks()
+    achieved = (wbytes + kvbytes) / (ms / 1e3) / 1e9
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+    agg = collections.defaultdict(lambda: [0, 0.0])
+    for e in prof.key_averages():
+        if e.device_time_total > 0:
+            agg[e.key][0] += e.count
+            agg[e.key][1] += e.device_time_total
+    tot = sum(v[1] for v in agg.values()) or 1.0
+    print("per-kernel device time of one decode step (3 graph replays, torch profiler):",
+          file=sys.stderr)
+    for k, (c, t) in sorted(agg.items(), key=lambda kv: -kv[1][1])[:20]:
+        print(f"  {t / 3 / 1000:8.3f} ms/step {100 * t / tot:5.1f}%  launches/step "
+              f"{c / 3:6.1f}  {k[:100]}", file=sys.stderr)
+    line = {
+        "metric": f"Qwen3-8B decode step ms (batch {B}, context {L})",
+        "value": round(ms, 4), "unit": "ms", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init N(0,0.02) weights, N(0,1) KV, random tables)",
+        "config": {"workload": "C4 decode step (CUDA graph)", "batch": B, "context": L,
+                   "l2": "weights + KV per step > L2"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "peak_source": f"{src} hbm_gbs",
+                     "kernel": "decode step (weights + KV bytes / step time)", "traffic": None},
+        "gpu_launches": per_step * args.steps,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["e2e", "decode", "prefill", "kvstore", "c5"],
+    ap.add_argument("--workload", choices=["e2e", "decode", "prefill", "kvstore", "c5", "c4step"],
                     default="e2e",
                     help="e2e (default): C4 Qwen3-8B output tok/s, tensor parallel over "
                          "--gpus; decode: C3 paged decode GB/s; prefill: C2 TFLOP/s; "
@@ -1092,6 +1191,8 @@ def main():
                     help="profiling only: B sequences of the C3 / C2 batch (e2e: requests)")
     ap.add_argument("--pool-blocks", type=int, default=None,
                     help="profiling only: KV pool size in blocks (C3 / C2)")
+    ap.add_argument("--context", type=int, default=840,
+                    help="c4step: context length of every decode row")
     ap.add_argument("--new-tokens", type=int, default=None,
                     help="profiling only (prefill): every sequence this many new tokens")
     ap.add_argument("--prefix-tokens", type=int, default=None,
@@ -1128,6 +1229,8 @@ def main():
             run_kvstore(args, rank, world, local_rank)
         elif args.workload in ("e2e", "c5"):
             run_e2e(args, rank, world, local_rank)
+        elif args.workload == "c4step":
+            run_c4step(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:
