@@ -954,7 +954,7 @@ def run_e2e(args, rank, world, local_rank):
                    max_num_seqs=cfg["max_num_seqs"], num_blocks=0, block_size=16,
                    tensor_parallel_size=tp, gpu_memory_utilization=0.9,
                    max_model_len=((max_len + 15) // 16) * 16, compat=False,
-                   enable_chunked_prefill=c5)
+                   enable_chunked_prefill=c5, fused_gemm_max_rows=args.fused_gemm)
 
     def progress(msg):
         print(f"[rank {rank}] {msg}", file=sys.stderr, flush=True)
@@ -1040,6 +1040,7 @@ def run_e2e(args, rank, world, local_rank):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded random token ids and lengths; random-init N(0,0.02) weights)",
         "config": {"workload": workload, "model": cfg["model"],
+                   "fused_gemm_max_rows": args.fused_gemm,
                    "step": "one Engine.generate() over the whole request set",
                    "num_requests": cfg["num_requests"], "output_tokens": out_tokens,
                    "prompt_tokens": sum(len(p) for p in all_prompts),
@@ -1094,6 +1095,8 @@ def run_c4step(args, rank, world, local_rank):
     cfg = get_config("Qwen3-8B")
     w = Qwen3Weights(cfg, dev, seed=0)
     m = Qwen3Model(w)
+    if args.fused_gemm:
+        m.enable_fused_gemm(args.fused_gemm)
     bs, D, Hkv = 16, cfg.head_dim, cfg.num_key_value_heads
     pages = (L + bs - 1) // bs
     nb = B * pages + 8
@@ -1157,6 +1160,7 @@ def run_c4step(args, rank, world, local_rank):
         "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init N(0,0.02) weights, N(0,1) KV, random tables)",
         "config": {"workload": "C4 decode step (CUDA graph)", "batch": B, "context": L,
+                   "fused_gemm_max_rows": args.fused_gemm,
                    "l2": "weights + KV per step > L2"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
@@ -1168,17 +1172,129 @@ def run_c4step(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def run_gemm(args, rank, world, local_rank):
+    """The four projections of one Qwen3-8B decoder layer at decode batch
+    sizes, cuBLAS (+ the separate K3 / SiLU-mul launches) against this
+    library's tcgen05 GEMMs with fused epilogues (vj_qkv_gemm_kv_store,
+    vj_decode_gemm PLAIN / SWIGLU). Four weight sets are cycled so that every
+    call streams its weights from HBM (4 x 50-200 MB > L2). Rows: --batch, or
+    a sweep of 1..512. CUDA events on the launching stream; one JSON line for
+    the largest row count, the per-op table on stderr."""
+    import torch
+    import torch.nn.functional as F
+    from vllm_b200.kernels.fused import silu_mul
+    from vllm_b200.kernels.gemm import decode_gemm, gemm_workspace_bytes, qkv_gemm_kv_store
+    from vllm_b200.kernels.kv_store import kv_store_qknorm_rope, rope_table
+    from vllm_b200.model.qwen3 import get_config
+    if world > 1:
+        raise SystemExit("--workload gemm runs on one GPU")
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    cfg = get_config("Qwen3-8B")
+    H, I, D = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
+    Hq, Hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+    NQKV = (Hq + 2 * Hkv) * D
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(11)
+    rnd = lambda *s, std=0.02: (torch.randn(s, generator=gen, device=dev) * std).to(torch.bfloat16)
+    sets = [dict(qkv=rnd(NQKV, H), o=rnd(H, Hq * D), gu=rnd(2 * I, H), down=rnd(H, I))
+            for _ in range(4)]
+    qn, kn = rnd(D, std=0.1) + 1, rnd(D, std=0.1) + 1
+    nb, bs = 4096, 16
+    cache = rnd(2, nb, bs, Hkv, D, std=1.0)
+    table = rope_table(dev, cfg.rope_theta, 4096)
+    rows_list = [args.batch] if args.batch else [1, 16, 64, 128, 256, 512]
+    maxr = max(rows_list)
+    ws = torch.zeros(max(gemm_workspace_bytes(r, n, k, m) for r in rows_list for n, k, m in
+                         ((NQKV, H, "plain"), (H, Hq * D, "plain"), (2 * I, H, "swiglu"),
+                          (H, I, "plain"))), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    reps = max(args.steps, 8)
+
+    def timed(fn):
+        for i in range(max(args.warmup, 3)):
+            fn(sets[i % 4])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(reps):
+            fn(sets[i % 4])
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps * 1e3   # us
+
+    results = {}
+    with ClockSampler(local_rank) as clk:
+        for R in rows_list:
+            x = rnd(R, H, std=1.0)
+            xo = rnd(R, Hq * D, std=1.0)
+            xi = rnd(R, I, std=1.0)
+            slots = torch.randperm(nb * bs, generator=gen, device=dev)[:R].to(torch.int32)
+            pos = torch.randint(0, 4000, (R,), generator=gen, device=dev).to(torch.int32)
+
+            def cub_qkv(s):
+                qkv = F.linear(x, s["qkv"])
+                q, k, v = torch.split(qkv, [Hq * D, Hkv * D, Hkv * D], -1)
+                kv_store_qknorm_rope(q.view(R, Hq, D), k.view(R, Hkv, D), v.view(R, Hkv, D),
+                                     cache, slots, pos, qn, kn, table=table)
+
+            def our_qkv(s):
+                qkv_gemm_kv_store(x, s["qkv"], cache, slots, pos, qn, kn, Hq, table=table, ws=ws)
+
+            ops = {
+                "qkv+K3": (cub_qkv, our_qkv, NQKV * H * 2),
+                "o_proj": (lambda s: F.linear(xo, s["o"]),
+                           lambda s: decode_gemm(xo, s["o"], ws=ws), H * Hq * D * 2),
+                "gate_up+SiLU": (lambda s: silu_mul(F.linear(x, s["gu"])),
+                                 lambda s: decode_gemm(x, s["gu"], "swiglu", ws=ws),
+                                 2 * I * H * 2),
+                "down": (lambda s: F.linear(xi, s["down"]),
+                         lambda s: decode_gemm(xi, s["down"], ws=ws), H * I * 2),
+            }
+            for name, (cub, ours, wb) in ops.items():
+                tc, to = timed(cub), timed(ours)
+                results[(R, name)] = (tc, to, wb)
+                print(f"rows {R:4d} {name:13s} cuBLAS {tc:8.2f} us ({wb / tc / 1e3:6.0f} GB/s)"
+                      f"   vj {to:8.2f} us ({wb / to / 1e3:6.0f} GB/s)  x{tc / to:5.2f}",
+                      file=sys.stderr)
+    peaks, src = load_peaks()
+    tot_c = sum(results[(maxr, n)][0] for n in ops)
+    tot_o = sum(results[(maxr, n)][1] for n in ops)
+    wbytes = sum(results[(maxr, n)][2] for n in ops)
+    line = {
+        "metric": f"Qwen3-8B decoder-layer projections us at {maxr} decode rows "
+                  "(qkv+K3, o_proj, gate_up+SiLU, down)",
+        "value": round(tot_o, 2), "unit": "us", "n_gpus": 1, "steps": reps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(tot_o / 1e3, 5),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random N(0,0.02) weights, N(0,1) activations)",
+        "config": {"workload": "decode-step GEMMs with fused epilogues", "rows": maxr,
+                   "cublas_plus_separate_kernels_us": round(tot_c, 2),
+                   "per_op_us": {n: [round(results[(maxr, n)][0], 2),
+                                     round(results[(maxr, n)][1], 2)] for n in ops},
+                   "l2": "4 weight sets cycled (> L2)"},
+        "roofline": {"bound": "hbm", "achieved": round(wbytes / tot_o / 1e3, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(wbytes / tot_o / 1e3 / peaks["hbm_gbs"], 4),
+                     "peak_source": f"{src} hbm_gbs", "kernel": "weights / time", "traffic": None},
+        "gpu_launches": 4 * reps * len(rows_list),
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["e2e", "decode", "prefill", "kvstore", "c5", "c4step"],
+    ap.add_argument("--workload", choices=["e2e", "decode", "prefill", "kvstore", "c5", "c4step",
+                                           "gemm"],
                     default="e2e",
                     help="e2e (default): C4 Qwen3-8B output tok/s, tensor parallel over "
                          "--gpus; decode: C3 paged decode GB/s; prefill: C2 TFLOP/s; "
-                         "kvstore: K3 GB/s; c5: Qwen3-32B chunked prefill tok/s")
+                         "kvstore: K3 GB/s; c5: Qwen3-32B chunked prefill tok/s; c4step: "
+                         "one decode step; gemm: decode-step projections vs cuBLAS")
     ap.add_argument("--model", default=None, help="e2e: model preset (default Qwen3-8B)")
     ap.add_argument("--max-num-seqs", type=int, default=None, help="e2e: scheduler seats")
     ap.add_argument("--tp", type=int, default=None,
@@ -1193,6 +1309,9 @@ def main():
                     help="profiling only: KV pool size in blocks (C3 / C2)")
     ap.add_argument("--context", type=int, default=840,
                     help="c4step: context length of every decode row")
+    ap.add_argument("--fused-gemm", type=int, default=0,
+                    help="e2e/c5/c4step: forwards of at most this many rows run their "
+                         "projections on the fused tcgen05 GEMMs (0: cuBLAS)")
     ap.add_argument("--new-tokens", type=int, default=None,
                     help="profiling only (prefill): every sequence this many new tokens")
     ap.add_argument("--prefix-tokens", type=int, default=None,
@@ -1231,6 +1350,8 @@ def main():
             run_e2e(args, rank, world, local_rank)
         elif args.workload == "c4step":
             run_c4step(args, rank, world, local_rank)
+        elif args.workload == "gemm":
+            run_gemm(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:

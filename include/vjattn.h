@@ -94,8 +94,9 @@ VJ_API int vj_version(void);
  *   [0, rope_table_len) (or rope_table_len == 0) are computed in the kernel
  * Slots outside [0, num_blocks*block_size) are dropped (after the optional
  * negative wrap). Numerics: per row, squares summed in fp32 in a fixed order
- * (each of the 16 lanes owning dims 8l..8l+7 sums its even and its odd dims
- * in dim order, adds the two, then a butterfly over lanes xor 8, 4, 2, 1);
+ * (each of 8 lanes owning dims 8l..8l+7 and 64+8l..64+8l+7 sums its even and
+ * its odd dims in dim order, adds the two, then a butterfly over lanes xor
+ * 4, 2, 1);
  * every later step is a correctly rounded fp32 op followed by bf16
  * round-to-nearest-even, so the result is reproducible bit for bit.
  * ------------------------------------------------------------------------- */
@@ -280,6 +281,52 @@ VJ_API vj_status vj_add_rmsnorm(const void *x, const void *residual,
                                 cudaStream_t stream);
 VJ_API vj_status vj_silu_mul(const void *gate_up, void *out, int64_t rows,
                              int32_t inter, cudaStream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Decode-step projections (tcgen05 GEMM, bf16 in, fp32 accumulate) with the
+ * next elementwise step fused into the epilogue. Built for decode batches
+ * (rows up to a few hundred; at most 65536): every weight byte is read once,
+ * the K dimension is split across CTAs as needed to fill the SMs, and split
+ * partials are summed in a fixed order (results do not depend on timing).
+ *
+ * vj_decode_gemm, w [n, k] bf16 row-major (an nn.Linear weight), x [rows, k]
+ * with row stride x_row_stride (0 -> k):
+ *   VJ_GEMM_PLAIN   out[rows, n] = bf16(x w^T)
+ *   VJ_GEMM_SWIGLU  w = [gate; up] (n = 2 I rows, I % 64 == 0):
+ *                   out[rows, I] = bf16(bf16(silu(bf16(x gate^T))) * bf16(x up^T)),
+ *                   the gate_up projection and vj_silu_mul in one launch
+ *                   (vllm/model/qwen3.py:337-341)
+ * vj_qkv_gemm_kv_store: the qkv projection (w_qkv = [Wq; Wk; Wv], rows
+ *   (Hq + 2 Hkv) * 128, k = hidden) followed in the epilogue by exactly
+ *   vj_kv_store_qknorm_rope's arithmetic on the bf16-rounded projections:
+ *   q/k RMSNorm, RoPE, q scaling, q written to q_out [rows, Hq, 128] and k/v
+ *   to their cache slots (qwen3.py:286-296, :105-111). Same flags and slot
+ *   rules as vj_kv_store_qknorm_rope; k_out is not produced.
+ * n and k: multiples of 128 and 64. splits: K split per output tile (0 ->
+ * chosen from the shape and the SM count; at most 32). workspace: at least
+ * vj_decode_gemm_workspace_size(rows, n, k, mode, splits) bytes (n = (Hq +
+ * 2 Hkv) * 128 and VJ_GEMM_PLAIN for the qkv call), 256-byte aligned and
+ * zero-filled once when allocated; calls leave it reusable (ticket words
+ * back at zero) unless error_flag (device int32, may be NULL) was set, after
+ * which it must be zero-filled again. A wait that runs out (2 s) sets
+ * *error_flag = 1 and the call's outputs are incomplete.
+ * ------------------------------------------------------------------------- */
+enum { VJ_GEMM_PLAIN = 0, VJ_GEMM_SWIGLU = 1 };
+
+VJ_API size_t vj_decode_gemm_workspace_size(int64_t rows, int32_t n, int32_t k, int32_t mode,
+                                            int32_t splits);
+VJ_API vj_status vj_decode_gemm(const void *x, int64_t x_row_stride, const void *w, void *out,
+                                int64_t out_row_stride, int64_t rows, int32_t n, int32_t k,
+                                int32_t mode, int32_t splits, void *workspace,
+                                size_t workspace_bytes, int32_t *error_flag, cudaStream_t stream);
+VJ_API vj_status vj_qkv_gemm_kv_store(
+    const void *x, int64_t x_row_stride, const void *w_qkv, const void *q_norm_w,
+    const void *k_norm_w, const int32_t *positions, const int32_t *slot_mapping, void *q_out,
+    void *k_cache, void *v_cache, int64_t num_tokens, int32_t hidden, int32_t num_q_heads,
+    int32_t num_kv_heads, int32_t head_dim, int64_t num_blocks, int32_t block_size,
+    int64_t stride_block, int64_t stride_token, int64_t stride_head, const void *rope_table,
+    int32_t rope_table_len, float eps, float rope_theta, int32_t flags, int32_t splits,
+    void *workspace, size_t workspace_bytes, int32_t *error_flag, cudaStream_t stream);
 
 /* ---------------------------------------------------------------------------
  * K4: batch metadata built on the GPU from device-resident engine state.

@@ -21,9 +21,11 @@ def _c1():
         return next(s for s in json.load(f) if s["name"] == "c1")
 
 
-@pytest.fixture(scope="module")
-def c1_run():
-    """Qwen3-0.6B, random weights (seed 0, drawn on the CPU), the C1 prompts."""
+@pytest.fixture(scope="module", params=[0, 64], ids=["cublas", "fused_gemm"])
+def c1_run(request):
+    """Qwen3-0.6B, random weights (seed 0, drawn on the CPU), the C1 prompts;
+    projections on cuBLAS + separate K3 / SiLU launches, or (fused_gemm) on
+    this library's tcgen05 GEMMs with fused epilogues for forwards of <= 64 rows."""
     from vllm_b200 import Config, SamplingParams
     from vllm_b200.model.qwen3 import PRESETS, Qwen3Weights
     from vllm_b200.src.engine import Engine
@@ -33,8 +35,8 @@ def c1_run():
     dev = torch.device("cuda", 0)
     weights = Qwen3Weights(cfg, dev, seed=0, gen_device="cpu")
     Request.reset_ids()
-    eng = Engine(Config(model="Qwen3-0.6B", **sc["config"]), dev, model_config=cfg,
-                 weights=weights, max_slots=16)
+    eng = Engine(Config(model="Qwen3-0.6B", fused_gemm_max_rows=request.param, **sc["config"]),
+                 dev, model_config=cfg, weights=weights, max_slots=16)
     outs = eng.generate(sc["prompts"], SamplingParams(temperature=0.0, max_new_tokens=32,
                                                       ignore_eos=True))
     return sc, cfg, weights, eng, outs

@@ -1,0 +1,639 @@
+// Decode-step projections on tcgen05 with their elementwise successors fused
+// into the epilogue:
+//
+//   vj_qkv_gemm_kv_store  q|k|v = x Wqkv^T, then in the epilogue K3's q/k
+//                         RMSNorm + interleaved-pair RoPE + q scaling + KV-slot
+//                         store (kv_row.cuh): the projected q/k/v rows never
+//                         reach HBM, and K3's launch disappears.
+//                         Replaces vllm/model/qwen3.py:286-296 (qkv projection,
+//                         q_norm/k_norm, apply_rope) and :105-111 (_update_kv_cache).
+//   vj_decode_gemm        out = x W^T (PLAIN), or SwiGLU: out = silu(x Wg^T) *
+//                         (x Wu^T) (qwen3.py:337-341), so the [T, 2I] gate/up
+//                         output and the separate SiLU-mul pass disappear.
+//
+// Shape: decode batches (T up to a few hundred rows) against weights of
+// 10^7-10^8 elements, so a launch is a weight stream: every weight byte is read
+// once from HBM; x (T x K bf16, at most a few MB) stays in L2.
+//
+// Tiling: a work unit is one 128-row x tile (m) x one 128-row weight tile (n)
+// x one contiguous range of the K blocks (split). Splits are chosen on the
+// host so that the units fill the SMs in whole waves; a persistent CTA per SM
+// walks units u = blockIdx.x, +gridDim.x, ... Consecutive units share their
+// weight tile (different m), so a weight tile comes from HBM once.
+//
+// CTA = 6 warps:
+//   warp 0      TMA producer: per K block one 128x64 x box and two 64x64
+//               weight boxes (128-byte swizzle) into a kStages-deep ring
+//   warp 1      TMEM owner + MMA issuer: tcgen05.mma kind::f16, M=N=128, K=16,
+//               both operands K-major in shared memory; the accumulator is
+//               double-buffered in TMEM (2 x 128 columns) so the epilogue of
+//               unit j overlaps the MMAs of unit j+1
+//   warps 2-5   epilogue, one accumulator row (TMEM lane) per thread
+// Split-K partials: every split writes its fp32 tile to the workspace, the
+// last of a tile's splits to arrive (atomicInc ticket, threadfence-reduction
+// pattern; no CTA ever waits for another) sums them in split order, so the
+// result does not depend on which split finished last.
+// Every mbarrier wait is bounded (2 s); a timeout sets the caller's error word.
+#include "../../include/vjattn.h"
+#include "vj_common.cuh"
+#include "kv_row.cuh"
+
+#include <algorithm>
+#include <string>
+
+namespace vj {
+namespace {
+
+constexpr int kBM = 128;           // x rows per tile
+constexpr int kBN = 128;           // weight rows per tile
+constexpr int kBK = 64;            // K elements per stage (one 128-byte swizzle row)
+constexpr int kStages = 5;
+constexpr int kTileBytes = kBM * kBK * 2;      // 16 KB
+constexpr int kStageBytes = 2 * kTileBytes;    // x tile + weight tile
+constexpr int kGemmThreads = 192;
+constexpr int kEpiThreads = 128;
+constexpr int kStagingBytes = kBM * 256;       // one bf16 128x128 tile (KV epilogue)
+constexpr int kMaxSplits = 32;
+
+enum { kModePlain = 0, kModeSwiglu = 1, kModeKv = 2 };
+
+struct GemmArgs {
+  int rows;                 // T
+  int kblocks;              // K / 64
+  int m_tiles, n_tiles, splits, units;
+  int mode;
+  int inter;                // SwiGLU: intermediate size I (gate rows [0,I), up rows [I,2I))
+  __nv_bfloat16 *out;       // PLAIN [T, N] / SwiGLU [T, I], row stride ldo
+  int64_t ldo;
+  float *partials;          // [tiles][splits][128 cols][128 rows] fp32 (splits > 1)
+  unsigned int *tickets;    // [tiles]
+  int *error;
+};
+
+struct Smem {
+  uint64_t full[kStages], empty[kStages];
+  uint64_t acc_full[2], acc_empty[2], drain;
+  uint32_t tmem_base;
+  int ticket;
+};
+constexpr int kOffStaging = kStages * kStageBytes;
+constexpr int kOffBars = kOffStaging + kStagingBytes;
+constexpr int kSmemBytes = kOffBars + static_cast<int>(sizeof(Smem)) + 1024;  // + alignment slack
+
+// Barrier among `count` threads that also ANDs their predicates, so that a
+// wait that ran out for some epilogue threads stops all of them together.
+VJ_DEV bool bar_and(uint32_t id, uint32_t count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
+VJ_DEV void flag_error(int *error) {
+  if (error) atomicExch(error, 1);
+}
+
+// Unit u -> (m tile, n tile, split); m fastest so that neighbouring CTAs
+// stream the same weight tile.
+VJ_DEV void unit_coords(const GemmArgs &g, int u, int &mt, int &nt, int &sp) {
+  mt = u % g.m_tiles;
+  const int r = u / g.m_tiles;
+  sp = r % g.splits;
+  nt = r / g.splits;
+}
+VJ_DEV int split_begin(const GemmArgs &g, int sp) {
+  return static_cast<int>((static_cast<int64_t>(sp) * g.kblocks) / g.splits);
+}
+
+// Weight rows of n tile nt: two 64-row boxes. PLAIN/KV: rows [128 nt, +128);
+// SwiGLU: gate rows [64 nt, +64) then up rows [I + 64 nt, +64), so the tile's
+// accumulator columns 0-63 are gate and 64-127 up for the same 64 outputs.
+VJ_DEV void weight_rows(const GemmArgs &g, int nt, int &r0, int &r1) {
+  if (g.mode == kModeSwiglu) {
+    r0 = 64 * nt;
+    r1 = g.inter + 64 * nt;
+  } else {
+    r0 = kBN * nt;
+    r1 = kBN * nt + 64;
+  }
+}
+
+// SiLU-mul of one output element, the same arithmetic as vj_silu_mul:
+// bf16(bf16(silu(g)) * u) with g, u the bf16-rounded projections.
+VJ_DEV float swiglu(float gate_acc, float up_acc) {
+  const float g = round_bf16(gate_acc);
+  const float u = round_bf16(up_acc);
+  const float s = round_bf16(g / (1.f + expf(-g)));
+  return s * u;
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
+                   const GemmArgs g, const KvArgs kv) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  Smem &sb = *reinterpret_cast<Smem *>(smem + kOffBars);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&sb.full[i], 1);
+      mbar_init(&sb.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sb.acc_full[i], 1);
+      mbar_init(&sb.acc_empty[i], kEpiThreads);
+    }
+    mbar_init(&sb.drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(&sb.tmem_base, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sb.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmx);
+      tma_prefetch_desc(&tmw);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < g.units && ok; u += gridDim.x) {
+        int mt, nt, sp;
+        unit_coords(g, u, mt, nt, sp);
+        int wr0, wr1;
+        weight_rows(g, nt, wr0, wr1);
+        const int kb1 = split_begin(g, sp + 1);
+        for (int kb = split_begin(g, sp); kb < kb1; ++kb, ++it) {
+          const int st = static_cast<int>(it % kStages);
+          if (it >= kStages && !mbar_wait(&sb.empty[st], ((it / kStages) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          uint8_t *dst = smem + st * kStageBytes;
+          mbar_arrive_expect_tx(&sb.full[st], kStageBytes);
+          tma_load_3d(dst, &tmx, &sb.full[st], kb * kBK, mt * kBM, 0);
+          tma_load_3d(dst + kTileBytes, &tmw, &sb.full[st], kb * kBK, wr0, 0);
+          tma_load_3d(dst + kTileBytes + kTileBytes / 2, &tmw, &sb.full[st], kb * kBK, wr1, 0);
+        }
+      }
+      if (!ok) {
+        flag_error(g.error);
+        // copies in flight must land before the CTA exits
+        for (uint32_t j = it > kStages ? it - kStages : 0; j < it; ++j) {
+          mbar_wait(&sb.full[j % kStages], (j / kStages) & 1);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(kBM, kBN, false);
+      const uint32_t s0 = smem_u32(smem);
+      uint32_t it = 0;
+      bool ok = true;
+      int j = 0;
+      for (int u = blockIdx.x; u < g.units && ok; u += gridDim.x, ++j) {
+        int mt, nt, sp;
+        unit_coords(g, u, mt, nt, sp);
+        const int buf = j & 1;
+        if (j >= 2 && !mbar_wait(&sb.acc_empty[buf], ((j >> 1) - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + buf * kBN;
+        const int kb0 = split_begin(g, sp), kb1 = split_begin(g, sp + 1);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int st = static_cast<int>(it % kStages);
+          if (!mbar_wait(&sb.full[st], (it / kStages) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t xa = s0 + st * kStageBytes, wa = xa + kTileBytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            umma_ss(d, umma_desc_sw128(xa + kk * 32, 16, 1024),
+                    umma_desc_sw128(wa + kk * 32, 16, 1024), idesc,
+                    (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&sb.empty[st]);
+        }
+        if (ok) umma_commit(&sb.acc_full[buf]);
+      }
+      if (!ok) flag_error(g.error);
+      // every issued MMA completes before TMEM is released
+      umma_commit(&sb.drain);
+      mbar_wait(&sb.drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int et = threadIdx.x - 64;                 // 0..127
+    const int quarter = warp & 3;                    // TMEM lane quarter of this warp
+    const int r = quarter * 32 + lane;               // accumulator row
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    uint8_t *staging = smem + kOffStaging;
+    // K3 state (KV mode): 16 groups of 8 lanes
+    const int grp = et >> 3, l8 = et & 7;
+    const unsigned grp_mask = 0xffu << (8 * (grp & 3));
+    RowSlice qw, kw;
+    if (g.mode == kModeKv) load_weights(kv, l8, qw, kw);
+    int j = 0;
+    for (int u = blockIdx.x; u < g.units; u += gridDim.x, ++j) {
+      int mt, nt, sp;
+      unit_coords(g, u, mt, nt, sp);
+      const int buf = j & 1;
+      if (!bar_and(1, kEpiThreads, mbar_wait(&sb.acc_full[buf], (j >> 1) & 1))) {
+        if (et == 0) flag_error(g.error);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t tacc = tmem + lane_addr + buf * kBN;
+      const int t = mt * kBM + r;
+      const bool live = t < g.rows;
+      const int tile = nt * g.m_tiles + mt;
+      const float *part = g.partials + static_cast<size_t>(tile) * g.splits * (kBM * kBN) + r;
+      if (g.splits > 1) {
+        // this split's partial tile to the workspace ([col][row]: coalesced);
+        // tcgen05.ld is warp-collective, so every lane loads
+        float *mine = g.partials + (static_cast<size_t>(tile) * g.splits + sp) * (kBM * kBN) + r;
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          float v[32];
+          tmem_ld32(tacc + c * 32, v);
+          if (live) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) __stcg(mine + (c * 32 + i) * kBM, v[i]);
+          }
+        }
+        __threadfence();
+        named_bar_sync(1, kEpiThreads);
+        if (et == 0) sb.ticket = static_cast<int>(atomicInc(g.tickets + tile, g.splits - 1));
+        named_bar_sync(1, kEpiThreads);
+        if (sb.ticket != g.splits - 1) {   // another split finishes this tile
+          tc_fence_before();
+          mbar_arrive(&sb.acc_empty[buf]);
+          continue;
+        }
+        __threadfence();
+      }
+      // columns [32c, 32c+32) of the finished row: this split's accumulator
+      // plus, with a K split, every split's partial summed in split order
+      auto chunk = [&](int c, float (&v)[32]) {
+        tmem_ld32(tacc + c * 32, v);
+        if (g.splits > 1 && live) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float *pc = part + static_cast<size_t>(c * 32 + i) * kBM;
+            float acc = sp == 0 ? v[i] : __ldcg(pc);
+            for (int q = 1; q < g.splits; ++q) {
+              acc += q == sp ? v[i] : __ldcg(pc + static_cast<size_t>(q) * (kBM * kBN));
+            }
+            v[i] = acc;
+          }
+        }
+      };
+
+      if (g.mode == kModePlain) {
+        uint4 *dst = reinterpret_cast<uint4 *>(g.out + static_cast<int64_t>(t) * g.ldo +
+                                               static_cast<int64_t>(nt) * kBN);
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          float v[32];
+          chunk(c, v);
+          if (live) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              dst[c * 4 + q] = make_uint4(pack_bf16(v[8 * q], v[8 * q + 1]),
+                                          pack_bf16(v[8 * q + 2], v[8 * q + 3]),
+                                          pack_bf16(v[8 * q + 4], v[8 * q + 5]),
+                                          pack_bf16(v[8 * q + 6], v[8 * q + 7]));
+            }
+          }
+        }
+      } else if (g.mode == kModeSwiglu) {
+        uint4 *dst = reinterpret_cast<uint4 *>(g.out + static_cast<int64_t>(t) * g.ldo +
+                                               static_cast<int64_t>(nt) * 64);
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          float gv[32], uv[32];
+          chunk(c, gv);        // gate columns [32c, 32c+32)
+          chunk(c + 2, uv);    // up columns of the same outputs
+          if (live) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint32_t w[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int e = 8 * q + 2 * i;
+                w[i] = pack_bf16(swiglu(gv[e], uv[e]), swiglu(gv[e + 1], uv[e + 1]));
+              }
+              dst[c * 4 + q] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        }
+      } else {
+        // KV: bf16 row into the staging tile (16-byte chunk c of row r at
+        // chunk c ^ (r & 15): conflict-free for both access patterns), then
+        // K3's 8-lane row code on 16 rows at a time
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          float v[32];
+          chunk(c, v);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint4 w = make_uint4(pack_bf16(v[8 * q], v[8 * q + 1]),
+                                       pack_bf16(v[8 * q + 2], v[8 * q + 3]),
+                                       pack_bf16(v[8 * q + 4], v[8 * q + 5]),
+                                       pack_bf16(v[8 * q + 6], v[8 * q + 7]));
+            const int ch = c * 4 + q;
+            *reinterpret_cast<uint4 *>(staging + r * 256 + ((ch ^ (r & 15)) << 4)) = w;
+          }
+        }
+        named_bar_sync(1, kEpiThreads);
+        const int h = nt;   // head row of q|k|v
+        const bool rotate = h < kv.Hq + kv.Hkv;
+        const bool do_norm = (kv.flags & VJ_KV_NORM) != 0;
+        const bool do_rope = (kv.flags & VJ_KV_ROPE) != 0;
+        const int qscale =
+            h < kv.Hq ? (kv.flags & (VJ_KV_QSCALE_DIV_SQRT_D | VJ_KV_QSCALE_MUL_RSQRT_D)) : 0;
+        for (int row = grp; row < kBM; row += kEpiThreads / 8) {
+          const int tr = mt * kBM + row;
+          if (tr >= g.rows) break;
+          const uint8_t *src = staging + row * 256;
+          const uint4 a = *reinterpret_cast<const uint4 *>(src + ((l8 ^ (row & 15)) << 4));
+          const uint4 b = *reinterpret_cast<const uint4 *>(src + (((8 + l8) ^ (row & 15)) << 4));
+          RowSlice x = {{a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w}};
+          if (rotate) {
+            RowSlice cs{};
+            if (do_rope) {
+              const int pos = __ldg(kv.positions + tr);
+              cs = (pos >= 0 && pos < kv.table_len)
+                       ? ldg_nc_slice(reinterpret_cast<const __nv_bfloat16 *>(
+                                          kv.rope_table + static_cast<int64_t>(pos) * 16), l8)
+                       : rope_slice(pos, kv.rope, l8);
+            }
+            norm_rope_row(x, h < kv.Hq ? qw : kw, cs, grp_mask, kv.eps, do_norm, do_rope, qscale);
+          }
+          store_row(kv, tr, h, h < kv.Hq ? 0 : __ldg(kv.slots + tr), x, l8);
+        }
+        named_bar_sync(1, kEpiThreads);   // staging free for the next unit
+      }
+      tc_fence_before();
+      mbar_arrive(&sb.acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 256);
+}
+
+}  // namespace
+
+namespace {
+
+struct GemmPlan {
+  int m_tiles, n_tiles, kblocks, splits, units, grid;
+};
+
+// Splits that minimise (waves of units) x (K blocks per unit + a fixed
+// per-unit cost of ~2 blocks for the pipeline fill and the epilogue).
+GemmPlan make_plan(int64_t rows, int n_tiles, int kblocks, int splits_req) {
+  GemmPlan p{};
+  p.m_tiles = static_cast<int>((rows + kBM - 1) / kBM);
+  p.n_tiles = n_tiles;
+  p.kblocks = kblocks;
+  const int sms = num_sms();
+  const int64_t tiles = static_cast<int64_t>(p.m_tiles) * n_tiles;
+  const int smax = std::min(kMaxSplits, kblocks);
+  int best = 1;
+  if (splits_req > 0) {
+    best = std::min(splits_req, smax);
+  } else {
+    int64_t best_cost = INT64_MAX;
+    for (int s = 1; s <= smax; ++s) {
+      const int64_t units = tiles * s;
+      const int64_t waves = (units + sms - 1) / sms;
+      const int64_t cost = waves * ((kblocks + s - 1) / s + 2);
+      if (cost < best_cost) {
+        best_cost = cost;
+        best = s;
+      }
+    }
+  }
+  p.splits = best;
+  p.units = static_cast<int>(tiles * best);
+  p.grid = std::min(p.units, sms);
+  return p;
+}
+
+size_t tickets_bytes(const GemmPlan &p) {
+  return (static_cast<size_t>(p.m_tiles) * p.n_tiles * sizeof(unsigned) + 255) & ~size_t(255);
+}
+size_t plan_workspace(const GemmPlan &p) {
+  size_t b = tickets_bytes(p);
+  if (p.splits > 1) {
+    b += static_cast<size_t>(p.m_tiles) * p.n_tiles * p.splits * kBM * kBN * sizeof(float);
+  }
+  return b;
+}
+
+int set_smem_attr() {
+  static bool done[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return set_error(VJ_ERR_CUDA, "cudaGetDevice failed");
+  if (dev >= 0 && dev < 64 && done[dev]) return VJ_OK;
+  if (cudaFuncSetAttribute(decode_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kSmemBytes) != cudaSuccess) {
+    return set_error(VJ_ERR_CUDA, "cudaFuncSetAttribute(decode_gemm_kernel) failed");
+  }
+  if (dev >= 0 && dev < 64) done[dev] = true;
+  return VJ_OK;
+}
+
+// Shared checks and launch. n_rows_w: weight rows; n_tiles per the mode.
+int launch_gemm(const char *who, const void *x, int64_t ldx, const void *w, int64_t n_rows_w,
+                int32_t k, int64_t rows, int n_tiles, GemmArgs &g, const KvArgs &kv,
+                int32_t splits, void *workspace, size_t workspace_bytes, int32_t *error_flag,
+                cudaStream_t stream) {
+  const std::string name(who);
+  if (k <= 0 || k % kBK != 0) {
+    return set_error(VJ_ERR_UNSUPPORTED, name + ": k must be a positive multiple of 64");
+  }
+  if (rows > 65536) return set_error(VJ_ERR_UNSUPPORTED, name + ": more than 65536 rows");
+  if (splits < 0) return set_error(VJ_ERR_INVALID_ARGUMENT, name + ": splits < 0");
+  if (!x || !w) return set_error(VJ_ERR_INVALID_ARGUMENT, name + ": null pointer");
+  if (ldx == 0) ldx = k;
+  if (ldx < k || ldx % 8 != 0 || reinterpret_cast<uintptr_t>(x) % 16 != 0 ||
+      reinterpret_cast<uintptr_t>(w) % 16 != 0) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT,
+                     name + ": x and w must be 16-byte aligned with rows of >= k elements, "
+                            "a multiple of 8");
+  }
+  const GemmPlan p = make_plan(rows, n_tiles, k / kBK, splits);
+  const size_t need = plan_workspace(p);
+  if (workspace == nullptr || workspace_bytes < need ||
+      reinterpret_cast<uintptr_t>(workspace) % 256 != 0) {
+    return set_error(VJ_ERR_WORKSPACE, name + ": workspace of " + std::to_string(need) +
+                                           " bytes (256-byte aligned) required");
+  }
+  CUtensorMap tmx, tmw;
+  int rc = encode_tmap_3d(&tmx, x, static_cast<uint64_t>(k), static_cast<uint64_t>(rows), 1,
+                          static_cast<uint64_t>(ldx) * 2, static_cast<uint64_t>(ldx) * 2 * rows,
+                          kBK, kBM, 1, true);
+  if (rc) return rc;
+  rc = encode_tmap_3d(&tmw, w, static_cast<uint64_t>(k), static_cast<uint64_t>(n_rows_w), 1,
+                      static_cast<uint64_t>(k) * 2, static_cast<uint64_t>(k) * 2 * n_rows_w, kBK,
+                      64, 1, true);
+  if (rc) return rc;
+  if ((rc = set_smem_attr()) != VJ_OK) return rc;
+  g.rows = static_cast<int>(rows);
+  g.kblocks = p.kblocks;
+  g.m_tiles = p.m_tiles;
+  g.n_tiles = p.n_tiles;
+  g.splits = p.splits;
+  g.units = p.units;
+  g.tickets = static_cast<unsigned *>(workspace);
+  g.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + tickets_bytes(p));
+  g.error = error_flag;
+  decode_gemm_kernel<<<p.grid, kGemmThreads, kSmemBytes, stream>>>(tmx, tmw, g, kv);
+  return check_launch(who);
+}
+
+}  // namespace
+}  // namespace vj
+
+extern "C" size_t vj_decode_gemm_workspace_size(int64_t rows, int32_t n, int32_t k, int32_t mode,
+                                                int32_t splits) {
+  using namespace vj;
+  if (rows <= 0 || n <= 0 || k <= 0 || k % kBK != 0 || splits < 0) return 0;
+  int n_tiles;
+  if (mode == VJ_GEMM_SWIGLU) {
+    if (n % 128 != 0) return 0;
+    n_tiles = n / 128;   // (n/2) / 64
+  } else {
+    if (n % kBN != 0) return 0;
+    n_tiles = n / kBN;
+  }
+  return plan_workspace(make_plan(rows, n_tiles, k / kBK, splits));
+}
+
+extern "C" vj_status vj_decode_gemm(const void *x, int64_t x_row_stride, const void *w, void *out,
+                                    int64_t out_row_stride, int64_t rows, int32_t n, int32_t k,
+                                    int32_t mode, int32_t splits, void *workspace,
+                                    size_t workspace_bytes, int32_t *error_flag,
+                                    cudaStream_t stream) {
+  using namespace vj;
+  if (rows < 0 || n <= 0) return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_decode_gemm: bad shape");
+  if (mode != VJ_GEMM_PLAIN && mode != VJ_GEMM_SWIGLU) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_decode_gemm: unknown mode");
+  }
+  if (n % 128 != 0) {
+    return set_error(VJ_ERR_UNSUPPORTED, "vj_decode_gemm: n must be a multiple of 128");
+  }
+  if (rows == 0) return VJ_OK;
+  const int64_t out_cols = mode == VJ_GEMM_SWIGLU ? n / 2 : n;
+  if (out_row_stride == 0) out_row_stride = out_cols;
+  if (!out || out_row_stride < out_cols || out_row_stride % 8 != 0 ||
+      reinterpret_cast<uintptr_t>(out) % 16 != 0) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT,
+                     "vj_decode_gemm: out must be 16-byte aligned with a row stride >= its "
+                     "columns, a multiple of 8");
+  }
+  GemmArgs g{};
+  g.mode = mode == VJ_GEMM_SWIGLU ? kModeSwiglu : kModePlain;
+  g.inter = static_cast<int>(n / 2);
+  g.out = static_cast<__nv_bfloat16 *>(out);
+  g.ldo = out_row_stride;
+  KvArgs kv{};
+  return launch_gemm("vj_decode_gemm", x, x_row_stride, w, n, k, rows,
+                     mode == VJ_GEMM_SWIGLU ? n / 128 : n / kBN, g, kv, splits, workspace,
+                     workspace_bytes, error_flag, stream);
+}
+
+extern "C" vj_status vj_qkv_gemm_kv_store(
+    const void *x, int64_t x_row_stride, const void *w_qkv, const void *q_norm_w,
+    const void *k_norm_w, const int32_t *positions, const int32_t *slot_mapping, void *q_out,
+    void *k_cache, void *v_cache, int64_t num_tokens, int32_t hidden, int32_t num_q_heads,
+    int32_t num_kv_heads, int32_t head_dim, int64_t num_blocks, int32_t block_size,
+    int64_t stride_block, int64_t stride_token, int64_t stride_head, const void *rope_table,
+    int32_t rope_table_len, float eps, float rope_theta, int32_t flags, int32_t splits,
+    void *workspace, size_t workspace_bytes, int32_t *error_flag, cudaStream_t stream) {
+  using namespace vj;
+  const char *who = "vj_qkv_gemm_kv_store";
+  if (num_tokens < 0 || num_q_heads < 0 || num_kv_heads <= 0 || num_blocks <= 0 ||
+      block_size <= 0 || rope_table_len < 0 || hidden <= 0) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_qkv_gemm_kv_store: negative or zero size");
+  }
+  if (head_dim != kHeadDim) {
+    return set_error(VJ_ERR_UNSUPPORTED, "vj_qkv_gemm_kv_store: head_dim must be 128");
+  }
+  if ((flags & VJ_KV_QSCALE_DIV_SQRT_D) && (flags & VJ_KV_QSCALE_MUL_RSQRT_D)) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_qkv_gemm_kv_store: choose one q scaling flag");
+  }
+  if (num_tokens == 0) return VJ_OK;
+  if (!slot_mapping || !k_cache || !v_cache || (num_q_heads > 0 && !q_out)) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_qkv_gemm_kv_store: null pointer");
+  }
+  if ((flags & VJ_KV_NORM) && ((num_q_heads > 0 && !q_norm_w) || !k_norm_w)) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_qkv_gemm_kv_store: VJ_KV_NORM needs norm weights");
+  }
+  if ((flags & VJ_KV_ROPE) && !positions) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_qkv_gemm_kv_store: VJ_KV_ROPE needs positions");
+  }
+  if (rope_table_len > 0 &&
+      (rope_table == nullptr || reinterpret_cast<uintptr_t>(rope_table) % 16 != 0)) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT,
+                     "vj_qkv_gemm_kv_store: rope_table must be 16-byte aligned");
+  }
+  if (reinterpret_cast<uintptr_t>(q_out) % 16 != 0 ||
+      ((flags & VJ_KV_NORM) && (reinterpret_cast<uintptr_t>(q_norm_w) |
+                                reinterpret_cast<uintptr_t>(k_norm_w)) % 16 != 0) ||
+      (stride_block | stride_token | stride_head) % 8 != 0 ||
+      (reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) % 16 != 0) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT,
+                     "vj_qkv_gemm_kv_store: q_out, norm weights and cache must be 16-byte "
+                     "aligned");
+  }
+  const int heads = num_q_heads + 2 * num_kv_heads;
+  GemmArgs g{};
+  g.mode = kModeKv;
+  KvArgs a{};
+  a.q_w = static_cast<const __nv_bfloat16 *>(q_norm_w);
+  a.k_w = static_cast<const __nv_bfloat16 *>(k_norm_w);
+  a.positions = positions;
+  a.slots = slot_mapping;
+  a.q_out = static_cast<__nv_bfloat16 *>(q_out);
+  a.k_out = nullptr;
+  a.k_cache = static_cast<__nv_bfloat16 *>(k_cache);
+  a.v_cache = static_cast<__nv_bfloat16 *>(v_cache);
+  a.rope_table = static_cast<const uint4 *>(rope_table);
+  a.table_len = rope_table_len > 0 ? rope_table_len : 0;
+  a.Hq = num_q_heads;
+  a.Hkv = num_kv_heads;
+  a.heads = heads;
+  a.num_slots = num_blocks * block_size;
+  a.block_size = block_size;
+  a.bs_shift = (block_size & (block_size - 1)) == 0 ? __builtin_ctz(block_size) : -1;
+  a.sb = stride_block;
+  a.st = stride_token;
+  a.sh = stride_head;
+  a.eps = eps;
+  a.flags = flags;
+  build_rope_table(rope_theta, a.rope.inv_freq);
+  return launch_gemm(who, x, x_row_stride, w_qkv, static_cast<int64_t>(heads) * kHeadDim, hidden,
+                     num_tokens, heads, g, a, splits, workspace, workspace_bytes, error_flag,
+                     stream);
+}

@@ -82,4 +82,4 @@ int num_sms() {
 
 extern "C" const char *vj_get_last_error(void) { return vj::g_last_error.c_str(); }
 
-extern "C" int vj_version(void) { return (2 << 16) | 0; }
+extern "C" int vj_version(void) { return (2 << 16) | 1; }

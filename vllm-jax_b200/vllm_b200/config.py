@@ -34,6 +34,12 @@ class Config:
     # step k+1 before reading step k's tokens back, so host work overlaps the
     # GPU; a request that samples EOS is computed one extra, discarded step.
     async_scheduling: bool = True
+    # Forward passes of at most this many rows (decode steps, small mixed
+    # steps) run their projections on this library's tcgen05 GEMMs with fused
+    # epilogues: qkv + q/k norm + RoPE + KV store in one launch, gate_up +
+    # SiLU-mul in one, o_proj / down_proj plain; larger ones use cuBLAS and the
+    # separate kernels. 0 turns the fused path off.
+    fused_gemm_max_rows: int = 0
 
     @property
     def max_len(self) -> int:

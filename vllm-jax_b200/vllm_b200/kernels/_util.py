@@ -40,8 +40,10 @@ def require_dtype(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
         raise ValueError(f"The dtype of `{name}` must be {dtype}. Got {t.dtype}")
 
 
-def workspace(device: torch.device, nbytes: int, tag: str = "decode") -> torch.Tensor:
-    """Per-device, per-tag scratch buffer that only grows (16-byte aligned).
+def workspace(device: torch.device, nbytes: int, tag: str = "decode",
+              zeroed: bool = False) -> torch.Tensor:
+    """Per-device, per-tag scratch buffer that only grows (256-byte aligned;
+    zero-filled when allocated if `zeroed`).
 
     A buffer that is outgrown is retired, never freed: a CUDA graph captured
     while it was current keeps its address and writes there on every replay."""
@@ -50,6 +52,7 @@ def workspace(device: torch.device, nbytes: int, tag: str = "decode") -> torch.T
     if buf is None or buf.numel() < nbytes:
         if buf is not None:
             _retired.append(buf)
-        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        alloc = torch.zeros if zeroed else torch.empty
+        buf = alloc(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _workspaces[key] = buf
     return buf

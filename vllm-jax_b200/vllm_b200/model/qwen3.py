@@ -28,6 +28,7 @@ import torch.nn.functional as F
 
 from ..kernels.decode_paged_attention import paged_decode
 from ..kernels.fused import add_rmsnorm, silu_mul
+from ..kernels.gemm import decode_gemm, gemm_workspace_bytes, qkv_gemm_kv_store
 from ..kernels.kv_store import kv_store_qknorm_rope
 from ..kernels.prefill_paged_attention import paged_attention_mixed, paged_prefill
 
@@ -221,6 +222,28 @@ class Qwen3Model:
         # split-KV scratch of the decode kernel, owned here so that captured
         # CUDA graphs keep a valid address (set by the model runner)
         self.decode_workspace: torch.Tensor | None = None
+        # forwards of at most this many rows use the fused tcgen05 projections
+        # (vj_qkv_gemm_kv_store, vj_decode_gemm); 0 = cuBLAS + separate kernels
+        self.fused_gemm_rows = 0
+        self.gemm_workspace: torch.Tensor | None = None
+
+    def enable_fused_gemm(self, max_rows: int) -> None:
+        """Use the fused projections for forwards of <= max_rows rows, with one
+        zero-filled workspace sized for every row count up to max_rows
+        (allocated here, before any CUDA graph capture, and never replaced)."""
+        c, w = self.cfg, self.w
+        H, D = c.hidden_size, self.d
+        I_l = w.layers[0].w_gate_up.shape[0] // 2
+        shapes = ((w.layers[0].w_qkv.shape[0], H, "plain"), (H, self.hq * D, "plain"),
+                  (2 * I_l, H, "swiglu"), (H, I_l, "plain"))
+        need = 256
+        for r in range(1, max_rows + 1):     # every row count: the split plan depends on it
+            need = max([need] + [gemm_workspace_bytes(r, n, k, m) for n, k, m in shapes])
+        self.gemm_workspace = torch.zeros(need, dtype=torch.uint8, device=w.layers[0].w_qkv.device)
+        self.fused_gemm_rows = max_rows
+
+    def _fused(self, T: int) -> bool:
+        return 0 < T <= self.fused_gemm_rows and self.gemm_workspace is not None
 
     def _all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         if self.pg is not None and self.w.tp_size > 1:
@@ -236,10 +259,15 @@ class Qwen3Model:
         T = a.shape[0]
         eps = self.cfg.rms_norm_eps
         c = self.tp_comm
+        fused = self._fused(T)
         if c is not None and T <= c.max_rows:
-            torch.mm(a, w.t(), out=c.buffer(site, T))
+            if fused:
+                decode_gemm(a, w, out=c.buffer(site, T), ws=self.gemm_workspace)
+            else:
+                torch.mm(a, w.t(), out=c.buffer(site, T))
             return c.allreduce_add_rmsnorm(site, T, x, w_norm, eps)
-        d = self._all_reduce(F.linear(a, w))
+        d = decode_gemm(a, w, ws=self.gemm_workspace) if fused else F.linear(a, w)
+        d = self._all_reduce(d)
         return add_rmsnorm(d, w_norm, eps, residual=x)
 
     def _layer(self, l: int, x: torch.Tensor, h: torch.Tensor, kv_cache: torch.Tensor, meta,
@@ -249,17 +277,29 @@ class Qwen3Model:
         lw = self.w.layers[l]
         c = self.cfg
         T = x.shape[0]
-        qkv = F.linear(h, lw.w_qkv)
-        q, k, v = torch.split(qkv, [self.hq * self.d, self.hkv * self.d, self.hkv * self.d], -1)
-        q = kv_store_qknorm_rope(q.view(T, self.hq, self.d), k.view(T, self.hkv, self.d),
-                                 v.view(T, self.hkv, self.d), kv_cache,
-                                 meta.slot_mapping, meta.positions, lw.q_norm, lw.k_norm,
-                                 eps=c.rms_norm_eps, rope_theta=c.rope_theta,
-                                 q_scale=q_scale, table=self.rope_table)
+        fused = self._fused(T)
+        if fused:
+            # qkv projection + q/k norm + RoPE + KV store in one launch
+            q = qkv_gemm_kv_store(h, lw.w_qkv, kv_cache, meta.slot_mapping, meta.positions,
+                                  lw.q_norm, lw.k_norm, self.hq, eps=c.rms_norm_eps,
+                                  rope_theta=c.rope_theta, q_scale=q_scale,
+                                  table=self.rope_table, ws=self.gemm_workspace)
+        else:
+            qkv = F.linear(h, lw.w_qkv)
+            q, k, v = torch.split(qkv, [self.hq * self.d, self.hkv * self.d, self.hkv * self.d],
+                                  -1)
+            q = kv_store_qknorm_rope(q.view(T, self.hq, self.d), k.view(T, self.hkv, self.d),
+                                     v.view(T, self.hkv, self.d), kv_cache,
+                                     meta.slot_mapping, meta.positions, lw.q_norm, lw.k_norm,
+                                     eps=c.rms_norm_eps, rope_theta=c.rope_theta,
+                                     q_scale=q_scale, table=self.rope_table)
         o = attn_fn(q, kv_cache).reshape(T, self.hq * self.d)
         # attn_output += x; post_attention_layernorm   (qwen3.py:375-389)
         x, h = self._reduce_add_norm(o, lw.w_o, x, lw.ln2, 0)
-        m = silu_mul(F.linear(h, lw.w_gate_up))
+        if fused:
+            m = decode_gemm(h, lw.w_gate_up, "swiglu", ws=self.gemm_workspace)
+        else:
+            m = silu_mul(F.linear(h, lw.w_gate_up))
         # outputs = residual + mlp; next input_layernorm (or the final norm)
         return self._reduce_add_norm(m, lw.w_down, x, w_next, 1)
 

@@ -88,6 +88,8 @@ class ModelRunner:
                                        model_cfg.num_attention_heads // tp_size,
                                        model_cfg.head_dim), 16),
             dtype=torch.uint8, device=device)
+        if config.fused_gemm_max_rows > 0:
+            self.model.enable_fused_gemm(config.fused_gemm_max_rows)
         hkv = model_cfg.num_key_value_heads // tp_size
         shape = (2, kv_cache_manager.num_blocks, config.block_size, hkv, model_cfg.head_dim)
         # zero-initialised like the reference's pool (model_runner.py:190-199)
