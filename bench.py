@@ -1178,8 +1178,9 @@ def run_gemm(args, rank, world, local_rank):
     library's tcgen05 GEMMs with fused epilogues (vj_qkv_gemm_kv_store,
     vj_decode_gemm PLAIN / SWIGLU). Four weight sets are cycled so that every
     call streams its weights from HBM (4 x 50-200 MB > L2). Rows: --batch, or
-    a sweep of 1..512. CUDA events on the launching stream; one JSON line for
-    the largest row count, the per-op table on stderr."""
+    a sweep of 1..512. Each op is timed as replays of a CUDA graph of --steps
+    calls (the engine's decode path), CUDA events on the launching stream;
+    one JSON line for the largest row count, the per-op table on stderr."""
     import torch
     import torch.nn.functional as F
     from vllm_b200.kernels.fused import silu_mul
@@ -1197,13 +1198,17 @@ def run_gemm(args, rank, world, local_rank):
     gen = torch.Generator(device=dev)
     gen.manual_seed(11)
     rnd = lambda *s, std=0.02: (torch.randn(s, generator=gen, device=dev) * std).to(torch.bfloat16)
+    from vllm_b200.kernels.gemm import TiledWeight
     sets = [dict(qkv=rnd(NQKV, H), o=rnd(H, Hq * D), gu=rnd(2 * I, H), down=rnd(H, I))
             for _ in range(4)]
+    for st in sets:   # the engine's decode path reads packed weight tiles
+        st.update(qkv_t=TiledWeight(st["qkv"]), o_t=TiledWeight(st["o"]),
+                  gu_t=TiledWeight(st["gu"], "swiglu"), down_t=TiledWeight(st["down"]))
     qn, kn = rnd(D, std=0.1) + 1, rnd(D, std=0.1) + 1
     nb, bs = 4096, 16
     cache = rnd(2, nb, bs, Hkv, D, std=1.0)
     table = rope_table(dev, cfg.rope_theta, 4096)
-    rows_list = [args.batch] if args.batch else [1, 16, 64, 128, 256, 512]
+    rows_list = [args.batch] if args.batch else [1, 8, 16, 32, 64, 128, 256, 512]
     maxr = max(rows_list)
     ws = torch.zeros(max(gemm_workspace_bytes(r, n, k, m) for r in rows_list for n, k, m in
                          ((NQKV, H, "plain"), (H, Hq * D, "plain"), (2 * I, H, "swiglu"),
@@ -1212,15 +1217,24 @@ def run_gemm(args, rank, world, local_rank):
     reps = max(args.steps, 8)
 
     def timed(fn):
+        """Device time of one call: `reps` calls captured in a CUDA graph (as
+        the engine runs decode steps), replayed 3 times after a warm-up."""
         for i in range(max(args.warmup, 3)):
             fn(sets[i % 4])
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(reps):
+                fn(sets[i % 4])
+        graph.replay()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for i in range(reps):
-            fn(sets[i % 4])
+        for _ in range(3):
+            graph.replay()
         e1.record(stream)
         torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / reps * 1e3   # us
+        del graph
+        return e0.elapsed_time(e1) / (3 * reps) * 1e3   # us
 
     results = {}
     with ClockSampler(local_rank) as clk:
@@ -1238,17 +1252,18 @@ def run_gemm(args, rank, world, local_rank):
                                      cache, slots, pos, qn, kn, table=table)
 
             def our_qkv(s):
-                qkv_gemm_kv_store(x, s["qkv"], cache, slots, pos, qn, kn, Hq, table=table, ws=ws)
+                qkv_gemm_kv_store(x, s["qkv_t"], cache, slots, pos, qn, kn, Hq, table=table,
+                                  ws=ws)
 
             ops = {
                 "qkv+K3": (cub_qkv, our_qkv, NQKV * H * 2),
                 "o_proj": (lambda s: F.linear(xo, s["o"]),
-                           lambda s: decode_gemm(xo, s["o"], ws=ws), H * Hq * D * 2),
+                           lambda s: decode_gemm(xo, s["o_t"], ws=ws), H * Hq * D * 2),
                 "gate_up+SiLU": (lambda s: silu_mul(F.linear(x, s["gu"])),
-                                 lambda s: decode_gemm(x, s["gu"], "swiglu", ws=ws),
+                                 lambda s: decode_gemm(x, s["gu_t"], "swiglu", ws=ws),
                                  2 * I * H * 2),
                 "down": (lambda s: F.linear(xi, s["down"]),
-                         lambda s: decode_gemm(xi, s["down"], ws=ws), H * I * 2),
+                         lambda s: decode_gemm(xi, s["down_t"], ws=ws), H * I * 2),
             }
             for name, (cub, ours, wb) in ops.items():
                 tc, to = timed(cub), timed(ours)

@@ -306,21 +306,35 @@ VJ_API vj_status vj_silu_mul(const void *gate_up, void *out, int64_t rows,
  * chosen from the shape and the SM count; at most 32). workspace: at least
  * vj_decode_gemm_workspace_size(rows, n, k, mode, splits) bytes (n = (Hq +
  * 2 Hkv) * 128 and VJ_GEMM_PLAIN for the qkv call), 256-byte aligned and
- * zero-filled once when allocated; calls leave it reusable (ticket words
- * back at zero) unless error_flag (device int32, may be NULL) was set, after
- * which it must be zero-filled again. A wait that runs out (2 s) sets
- * *error_flag = 1 and the call's outputs are incomplete.
+ * zero-filled once when allocated. Its first 64 KB hold the split tickets
+ * (one word per output tile, whatever the shape), the fp32 split partials
+ * follow, so one workspace serves calls of any shapes in stream order; calls
+ * leave the tickets at zero unless error_flag (device int32, may be NULL) was
+ * set, after which the workspace must be zero-filled again. A wait that runs
+ * out (2 s) sets *error_flag = 1 and the call's outputs are incomplete.
  * ------------------------------------------------------------------------- */
 enum { VJ_GEMM_PLAIN = 0, VJ_GEMM_SWIGLU = 1 };
+/* weight_layout: VJ_WEIGHTS_ROW_MAJOR (w as given, read through a TMA tensor
+ * map) or VJ_WEIGHTS_TILED (w packed once by vj_pack_weight_tiles with the
+ * same n, k and mode; every pipeline stage is then one contiguous 16 KB bulk
+ * copy, the faster weight stream). Both give bit-identical results. */
+enum { VJ_WEIGHTS_ROW_MAJOR = 0, VJ_WEIGHTS_TILED = 1 };
 
 VJ_API size_t vj_decode_gemm_workspace_size(int64_t rows, int32_t n, int32_t k, int32_t mode,
                                             int32_t splits);
-VJ_API vj_status vj_decode_gemm(const void *x, int64_t x_row_stride, const void *w, void *out,
-                                int64_t out_row_stride, int64_t rows, int32_t n, int32_t k,
-                                int32_t mode, int32_t splits, void *workspace,
-                                size_t workspace_bytes, int32_t *error_flag, cudaStream_t stream);
+/* Pack w [n, k] (mode VJ_GEMM_PLAIN, or VJ_GEMM_SWIGLU for [gate; up]) into
+ * out (n * k bf16, distinct from w): 16 KB blocks of 128 weight rows x 64 K
+ * in shared-memory swizzle order. */
+VJ_API vj_status vj_pack_weight_tiles(const void *w, void *out, int32_t n, int32_t k,
+                                      int32_t mode, cudaStream_t stream);
+VJ_API vj_status vj_decode_gemm(const void *x, int64_t x_row_stride, const void *w,
+                                int32_t weight_layout, void *out, int64_t out_row_stride,
+                                int64_t rows, int32_t n, int32_t k, int32_t mode, int32_t splits,
+                                void *workspace, size_t workspace_bytes, int32_t *error_flag,
+                                cudaStream_t stream);
 VJ_API vj_status vj_qkv_gemm_kv_store(
-    const void *x, int64_t x_row_stride, const void *w_qkv, const void *q_norm_w,
+    const void *x, int64_t x_row_stride, const void *w_qkv, int32_t weight_layout,
+    const void *q_norm_w,
     const void *k_norm_w, const int32_t *positions, const int32_t *slot_mapping, void *q_out,
     void *k_cache, void *v_cache, int64_t num_tokens, int32_t hidden, int32_t num_q_heads,
     int32_t num_kv_heads, int32_t head_dim, int64_t num_blocks, int32_t block_size,

@@ -67,20 +67,25 @@ def test_validation_without_gpu():
     assert lib.vj_paged_decode_workspace_size(256, 32, 128, 0) > 0
     assert lib.vj_paged_decode_workspace_size(256, 32, 64, 0) == 0
     # decode GEMMs: qkv of Qwen3-8B at 128 rows splits K in 3 (48 tiles x 3 =
-    # 144 units on 148 SMs): 256 B of tickets + 48 x 3 fp32 128x128 partials
+    # 144 units on 148 SMs): the 64 KB ticket area + 48 x 3 fp32 128x128 partials
     assert lib.vj_decode_gemm_workspace_size(128, 6144, 4096, _native.VJ_GEMM_PLAIN, 0) == \
-        256 + 48 * 3 * 128 * 128 * 4
-    assert lib.vj_decode_gemm_workspace_size(128, 6144, 4096, _native.VJ_GEMM_PLAIN, 1) == 256
+        65536 + 48 * 3 * 128 * 128 * 4
+    assert lib.vj_decode_gemm_workspace_size(128, 6144, 4096, _native.VJ_GEMM_PLAIN, 1) == 65536
     assert lib.vj_decode_gemm_workspace_size(128, 6144, 100, _native.VJ_GEMM_PLAIN, 0) == 0
-    st = lib.vj_decode_gemm(16, 0, 16, 16, 0, 4, 256, 100, _native.VJ_GEMM_PLAIN, 0, 16, 1 << 20,
-                            None, None)
+    st = lib.vj_decode_gemm(16, 0, 16, 0, 16, 0, 4, 256, 100, _native.VJ_GEMM_PLAIN, 0, 16,
+                            1 << 20, None, None)
     assert st == _native.VJ_ERR_UNSUPPORTED and b"multiple of 64" in lib.vj_get_last_error()
-    st = lib.vj_decode_gemm(16, 0, 16, 16, 0, 4, 256, 128, 7, 0, 16, 1 << 20, None, None)
+    st = lib.vj_decode_gemm(16, 0, 16, 0, 16, 0, 4, 256, 128, 7, 0, 16, 1 << 20, None, None)
     assert st == _native.VJ_ERR_INVALID_ARGUMENT
-    st = lib.vj_decode_gemm(16, 0, 16, 16, 0, 4, 256, 128, _native.VJ_GEMM_PLAIN, 0, 16, 64,
+    st = lib.vj_decode_gemm(16, 0, 16, 0, 16, 0, 4, 256, 128, _native.VJ_GEMM_PLAIN, 0, 16, 64,
                             None, None)
     assert st == _native.VJ_ERR_WORKSPACE
-    st = lib.vj_qkv_gemm_kv_store(16, 0, 16, 16, 16, 16, 16, 16, 16, 16, 4, 4096, 32, 8, 64,
+    st = lib.vj_decode_gemm(16, 0, 16, 5, 16, 0, 4, 256, 128, _native.VJ_GEMM_PLAIN, 0, 256,
+                            1 << 20, None, None)
+    assert st == _native.VJ_ERR_INVALID_ARGUMENT and b"weight_layout" in lib.vj_get_last_error()
+    assert lib.vj_pack_weight_tiles(16, 32, 100, 64, 0, None) == _native.VJ_ERR_UNSUPPORTED
+    assert lib.vj_pack_weight_tiles(16, 16, 128, 64, 0, None) == _native.VJ_ERR_INVALID_ARGUMENT
+    st = lib.vj_qkv_gemm_kv_store(16, 0, 16, 0, 16, 16, 16, 16, 16, 16, 16, 4, 4096, 32, 8, 64,
                                   16, 16, 4096, 256, 128, None, 0, 1e-6, 1e6, 0, 0, 16, 1 << 20,
                                   None, None)
     assert st == _native.VJ_ERR_UNSUPPORTED and b"head_dim" in lib.vj_get_last_error()

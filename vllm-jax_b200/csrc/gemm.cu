@@ -15,24 +15,34 @@
 // 10^7-10^8 elements, so a launch is a weight stream: every weight byte is read
 // once from HBM; x (T x K bf16, at most a few MB) stays in L2.
 //
-// Tiling: a work unit is one 128-row x tile (m) x one 128-row weight tile (n)
-// x one contiguous range of the K blocks (split). Splits are chosen on the
-// host so that the units fill the SMs in whole waves; a persistent CTA per SM
-// walks units u = blockIdx.x, +gridDim.x, ... Consecutive units share their
-// weight tile (different m), so a weight tile comes from HBM once.
+// Operand roles ("swap AB"): the MMA's M side is 128 weight rows (output
+// features), its N side the call's tokens, padded to a multiple of 16 (at most
+// 128 per m tile), so a batch of 8 tokens moves and multiplies 16 token rows,
+// not 128. D^T[feature, token] accumulates in TMEM, one feature per lane.
+//
+// Tiling: a work unit is one 128-row weight tile (n) x one tile of <= 128
+// tokens (m) x one contiguous range of the K blocks (split). Splits are chosen
+// on the host so that the units fill the SMs in whole waves; a persistent CTA
+// per SM walks units u = blockIdx.x, +gridDim.x, ... Consecutive units share
+// their weight tile (different m), so a weight tile comes from HBM once.
 //
 // CTA = 6 warps:
-//   warp 0      TMA producer: per K block one 128x64 x box and two 64x64
-//               weight boxes (128-byte swizzle) into a kStages-deep ring
-//   warp 1      TMEM owner + MMA issuer: tcgen05.mma kind::f16, M=N=128, K=16,
-//               both operands K-major in shared memory; the accumulator is
-//               double-buffered in TMEM (2 x 128 columns) so the epilogue of
-//               unit j overlaps the MMAs of unit j+1
-//   warps 2-5   epilogue, one accumulator row (TMEM lane) per thread
-// Split-K partials: every split writes its fp32 tile to the workspace, the
-// last of a tile's splits to arrive (atomicInc ticket, threadfence-reduction
-// pattern; no CTA ever waits for another) sums them in split order, so the
-// result does not depend on which split finished last.
+//   warp 0      TMA producer: per K block two 64x64 weight boxes and one x box
+//               (n_pad tokens x 64), 128-byte swizzle, into a ring of up to 12
+//               stages in 192 KB
+//   warp 1      TMEM owner + MMA issuer: tcgen05.mma kind::f16, M = 128,
+//               N = n_pad, K = 16, both operands K-major in shared memory; the
+//               256 TMEM columns hold 2 (n_pad > 64), 4 (> 32) or 8
+//               accumulators, so the MMAs run that many units ahead of the
+//               epilogue
+//   warps 2-5   epilogue: lane f holds feature f of every token; with a K
+//               split the fp32 partials go through the workspace (the last of
+//               a tile's splits to arrive -- atomicInc ticket, threadfence-
+//               reduction pattern, no CTA ever waits for another -- sums them
+//               in split order, so results do not depend on timing); the bf16
+//               tile is transposed into a [token][feature] shared-memory tile,
+//               from which the mode's row pass stores (PLAIN), applies SiLU-mul
+//               (SWIGLU) or runs K3's 8-lane row code (KV)
 // Every mbarrier wait is bounded (2 s); a timeout sets the caller's error word.
 #include "../../include/vjattn.h"
 #include "vj_common.cuh"
@@ -44,16 +54,21 @@
 namespace vj {
 namespace {
 
-constexpr int kBM = 128;           // x rows per tile
-constexpr int kBN = 128;           // weight rows per tile
+constexpr int kBM = 128;           // tokens per m tile (MMA N at most)
+constexpr int kBN = 128;           // weight rows per tile (MMA M)
 constexpr int kBK = 64;            // K elements per stage (one 128-byte swizzle row)
-constexpr int kStages = 5;
-constexpr int kTileBytes = kBM * kBK * 2;      // 16 KB
-constexpr int kStageBytes = 2 * kTileBytes;    // x tile + weight tile
+constexpr int kMaxStages = 12;
+constexpr int kTileBytes = kBN * kBK * 2;      // 16 KB: the weight tile of a K block
+constexpr int kRingBytes = 192 * 1024;         // stages: [weight tile][x box]
 constexpr int kGemmThreads = 192;
 constexpr int kEpiThreads = 128;
-constexpr int kStagingBytes = kBM * 256;       // one bf16 128x128 tile (KV epilogue)
+constexpr int kStagingBytes = kBM * 256;       // one bf16 [token][feature] tile
 constexpr int kMaxSplits = 32;
+// The workspace starts with a fixed ticket area (one word per output tile of
+// a split-K call), the same for every shape, so that calls of different shapes
+// sharing one workspace never write partials over another call's tickets.
+constexpr int kMaxTicketTiles = 16384;
+constexpr size_t kTicketBytes = kMaxTicketTiles * sizeof(unsigned);
 
 enum { kModePlain = 0, kModeSwiglu = 1, kModeKv = 2 };
 
@@ -61,22 +76,27 @@ struct GemmArgs {
   int rows;                 // T
   int kblocks;              // K / 64
   int m_tiles, n_tiles, splits, units;
+  int n_pad;                // tokens per m tile rounded up to 16 (MMA N), <= 128
+  int nbuf;                 // TMEM accumulators (256 / nbuf columns each)
   int mode;
+  int stages;               // ring depth
+  int stage_bytes;          // 16 KB of weights + n_pad x 128 B of x
   int inter;                // SwiGLU: intermediate size I (gate rows [0,I), up rows [I,2I))
+  const uint8_t *wtiles;    // weights packed by vj_pack_weight_tiles (or NULL: tensor map)
   __nv_bfloat16 *out;       // PLAIN [T, N] / SwiGLU [T, I], row stride ldo
   int64_t ldo;
-  float *partials;          // [tiles][splits][128 cols][128 rows] fp32 (splits > 1)
+  float *partials;          // [tiles][splits][128 tokens][128 features] fp32 (splits > 1)
   unsigned int *tickets;    // [tiles]
   int *error;
 };
 
 struct Smem {
-  uint64_t full[kStages], empty[kStages];
-  uint64_t acc_full[2], acc_empty[2], drain;
+  uint64_t full[kMaxStages], empty[kMaxStages];
+  uint64_t acc_full[8], acc_empty[8], drain;
   uint32_t tmem_base;
   int ticket;
 };
-constexpr int kOffStaging = kStages * kStageBytes;
+constexpr int kOffStaging = kRingBytes;
 constexpr int kOffBars = kOffStaging + kStagingBytes;
 constexpr int kSmemBytes = kOffBars + static_cast<int>(sizeof(Smem)) + 1024;  // + alignment slack
 
@@ -113,7 +133,7 @@ VJ_DEV int split_begin(const GemmArgs &g, int sp) {
 
 // Weight rows of n tile nt: two 64-row boxes. PLAIN/KV: rows [128 nt, +128);
 // SwiGLU: gate rows [64 nt, +64) then up rows [I + 64 nt, +64), so the tile's
-// accumulator columns 0-63 are gate and 64-127 up for the same 64 outputs.
+// features 0-63 are gate and 64-127 up for the same 64 outputs.
 VJ_DEV void weight_rows(const GemmArgs &g, int nt, int &r0, int &r1) {
   if (g.mode == kModeSwiglu) {
     r0 = 64 * nt;
@@ -126,11 +146,18 @@ VJ_DEV void weight_rows(const GemmArgs &g, int nt, int &r0, int &r1) {
 
 // SiLU-mul of one output element, the same arithmetic as vj_silu_mul:
 // bf16(bf16(silu(g)) * u) with g, u the bf16-rounded projections.
-VJ_DEV float swiglu(float gate_acc, float up_acc) {
-  const float g = round_bf16(gate_acc);
-  const float u = round_bf16(up_acc);
+VJ_DEV float swiglu(float gate, float up) {
+  const float g = round_bf16(gate);
+  const float u = round_bf16(up);
   const float s = round_bf16(g / (1.f + expf(-g)));
   return s * u;
+}
+
+// Byte offset of (token row t, 16-byte chunk c) in the staging tile: chunk c
+// of row t sits at chunk c ^ (t & 15), so that a warp writing 32 features of
+// one token and 8 lanes reading 8 chunks of one row both hit distinct banks.
+VJ_DEV uint32_t stg_off(int t, int c) {
+  return static_cast<uint32_t>(t) * 256u + (static_cast<uint32_t>(c ^ (t & 15)) << 4);
 }
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -143,11 +170,11 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < g.stages; ++i) {
       mbar_init(&sb.full[i], 1);
       mbar_init(&sb.empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < g.nbuf; ++i) {
       mbar_init(&sb.acc_full[i], 1);
       mbar_init(&sb.acc_empty[i], kEpiThreads);
     }
@@ -159,12 +186,13 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sb.tmem_base;
+  const uint32_t S = static_cast<uint32_t>(g.stages);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&tmx);
-      tma_prefetch_desc(&tmw);
+      if (g.wtiles == nullptr) tma_prefetch_desc(&tmw);
       uint32_t it = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < g.units && ok; u += gridDim.x) {
@@ -174,30 +202,37 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
         weight_rows(g, nt, wr0, wr1);
         const int kb1 = split_begin(g, sp + 1);
         for (int kb = split_begin(g, sp); kb < kb1; ++kb, ++it) {
-          const int st = static_cast<int>(it % kStages);
-          if (it >= kStages && !mbar_wait(&sb.empty[st], ((it / kStages) - 1) & 1)) {
+          const int st = static_cast<int>(it % S);
+          if (it >= S && !mbar_wait(&sb.empty[st], ((it / S) - 1) & 1)) {
             ok = false;
             break;
           }
-          uint8_t *dst = smem + st * kStageBytes;
-          mbar_arrive_expect_tx(&sb.full[st], kStageBytes);
-          tma_load_3d(dst, &tmx, &sb.full[st], kb * kBK, mt * kBM, 0);
-          tma_load_3d(dst + kTileBytes, &tmw, &sb.full[st], kb * kBK, wr0, 0);
-          tma_load_3d(dst + kTileBytes + kTileBytes / 2, &tmw, &sb.full[st], kb * kBK, wr1, 0);
+          uint8_t *dst = smem + st * g.stage_bytes;
+          mbar_arrive_expect_tx(&sb.full[st], g.stage_bytes);
+          if (g.wtiles != nullptr) {
+            // packed weights: the stage's 16 KB tile is one contiguous block,
+            // already in the swizzled order, moved by one bulk copy
+            bulk_g2s(dst, g.wtiles + (static_cast<size_t>(nt) * g.kblocks + kb) * kTileBytes,
+                     kTileBytes, &sb.full[st]);
+          } else {
+            tma_load_3d(dst, &tmw, &sb.full[st], kb * kBK, wr0, 0);
+            tma_load_3d(dst + kTileBytes / 2, &tmw, &sb.full[st], kb * kBK, wr1, 0);
+          }
+          tma_load_3d(dst + kTileBytes, &tmx, &sb.full[st], kb * kBK, mt * kBM, 0);
         }
       }
       if (!ok) {
         flag_error(g.error);
         // copies in flight must land before the CTA exits
-        for (uint32_t j = it > kStages ? it - kStages : 0; j < it; ++j) {
-          mbar_wait(&sb.full[j % kStages], (j / kStages) & 1);
+        for (uint32_t j = it > S ? it - S : 0; j < it; ++j) {
+          mbar_wait(&sb.full[j % S], (j / S) & 1);
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(kBM, kBN, false);
+      const uint32_t idesc = umma_idesc_bf16(kBN, g.n_pad, false);
       const uint32_t s0 = smem_u32(smem);
       uint32_t it = 0;
       bool ok = true;
@@ -205,26 +240,26 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
       for (int u = blockIdx.x; u < g.units && ok; u += gridDim.x, ++j) {
         int mt, nt, sp;
         unit_coords(g, u, mt, nt, sp);
-        const int buf = j & 1;
-        if (j >= 2 && !mbar_wait(&sb.acc_empty[buf], ((j >> 1) - 1) & 1)) {
+        const int buf = j % g.nbuf;
+        if (j >= g.nbuf && !mbar_wait(&sb.acc_empty[buf], ((j / g.nbuf) - 1) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem + buf * kBN;
+        const uint32_t d = tmem + buf * (256 / g.nbuf);
         const int kb0 = split_begin(g, sp), kb1 = split_begin(g, sp + 1);
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const int st = static_cast<int>(it % kStages);
-          if (!mbar_wait(&sb.full[st], (it / kStages) & 1)) {
+          const int st = static_cast<int>(it % S);
+          if (!mbar_wait(&sb.full[st], (it / S) & 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t xa = s0 + st * kStageBytes, wa = xa + kTileBytes;
+          const uint32_t wa = s0 + st * g.stage_bytes, xa = wa + kTileBytes;
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            umma_ss(d, umma_desc_sw128(xa + kk * 32, 16, 1024),
-                    umma_desc_sw128(wa + kk * 32, 16, 1024), idesc,
+            umma_ss(d, umma_desc_sw128(wa + kk * 32, 16, 1024),
+                    umma_desc_sw128(xa + kk * 32, 16, 1024), idesc,
                     (kb > kb0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&sb.empty[st]);
@@ -240,7 +275,7 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
     // ------------------------------------------------------------ epilogue
     const int et = threadIdx.x - 64;                 // 0..127
     const int quarter = warp & 3;                    // TMEM lane quarter of this warp
-    const int r = quarter * 32 + lane;               // accumulator row
+    const int f = quarter * 32 + lane;               // feature (weight row) of the tile
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     uint8_t *staging = smem + kOffStaging;
     // K3 state (KV mode): 16 groups of 8 lanes
@@ -248,32 +283,33 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
     const unsigned grp_mask = 0xffu << (8 * (grp & 3));
     RowSlice qw, kw;
     if (g.mode == kModeKv) load_weights(kv, l8, qw, kw);
+    const int nchunks = (g.n_pad + 31) / 32;
     int j = 0;
     for (int u = blockIdx.x; u < g.units; u += gridDim.x, ++j) {
       int mt, nt, sp;
       unit_coords(g, u, mt, nt, sp);
-      const int buf = j & 1;
-      if (!bar_and(1, kEpiThreads, mbar_wait(&sb.acc_full[buf], (j >> 1) & 1))) {
+      const int buf = j % g.nbuf;
+      if (!bar_and(1, kEpiThreads, mbar_wait(&sb.acc_full[buf], (j / g.nbuf) & 1))) {
         if (et == 0) flag_error(g.error);
         break;
       }
       tc_fence_after();
-      const uint32_t tacc = tmem + lane_addr + buf * kBN;
-      const int t = mt * kBM + r;
-      const bool live = t < g.rows;
+      const uint32_t tacc = tmem + lane_addr + buf * (256 / g.nbuf);
+      const int nlive = min(kBM, g.rows - mt * kBM);     // tokens of this m tile
       const int tile = nt * g.m_tiles + mt;
-      const float *part = g.partials + static_cast<size_t>(tile) * g.splits * (kBM * kBN) + r;
+      const float *part = g.partials + static_cast<size_t>(tile) * g.splits * (kBM * kBN) + f;
       if (g.splits > 1) {
-        // this split's partial tile to the workspace ([col][row]: coalesced);
-        // tcgen05.ld is warp-collective, so every lane loads
-        float *mine = g.partials + (static_cast<size_t>(tile) * g.splits + sp) * (kBM * kBN) + r;
+        // this split's partial tile to the workspace ([token][feature]:
+        // coalesced); tcgen05.ld is warp-collective, so every lane loads
 #pragma unroll 1
-        for (int c = 0; c < kBN / 32; ++c) {
+        for (int c = 0; c < nchunks; ++c) {
           float v[32];
           tmem_ld32(tacc + c * 32, v);
-          if (live) {
+          float *mine = g.partials + (static_cast<size_t>(tile) * g.splits + sp) * (kBM * kBN) +
+                        static_cast<size_t>(c * 32) * kBN + f;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) __stcg(mine + (c * 32 + i) * kBM, v[i]);
+          for (int i = 0; i < 32; ++i) {
+            if (c * 32 + i < nlive) __stcg(mine + i * kBN, v[i]);
           }
         }
         __threadfence();
@@ -287,92 +323,97 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
         }
         __threadfence();
       }
-      // columns [32c, 32c+32) of the finished row: this split's accumulator
-      // plus, with a K split, every split's partial summed in split order
-      auto chunk = [&](int c, float (&v)[32]) {
+      // feature f of tokens [32c, 32c+32): this split's accumulator plus,
+      // with a K split, every split's partial in split order; each split's
+      // 16 values are loaded together, the next split's while the current
+      // ones are added. The bf16 results go to the staging tile.
+#pragma unroll 1
+      for (int c = 0; c < nchunks; ++c) {
+        float v[32];
         tmem_ld32(tacc + c * 32, v);
-        if (g.splits > 1 && live) {
+        if (g.splits > 1) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float *pc = part + static_cast<size_t>(c * 32 + i) * kBM;
-            float acc = sp == 0 ? v[i] : __ldcg(pc);
-            for (int q = 1; q < g.splits; ++q) {
-              acc += q == sp ? v[i] : __ldcg(pc + static_cast<size_t>(q) * (kBM * kBN));
+          for (int h = 0; h < 2; ++h) {
+            const int t0 = c * 32 + h * 16;
+            if (t0 >= nlive) break;
+            const float *pc = part + static_cast<size_t>(t0) * kBN;
+            float acc[16], cur[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              cur[i] = (sp == 0 || t0 + i >= nlive) ? v[h * 16 + i] : __ldcg(pc + i * kBN);
             }
-            v[i] = acc;
+#pragma unroll 1
+            for (int q = 0; q < g.splits; ++q) {
+              float nxt[16];
+              const int qn = q + 1;
+              if (qn < g.splits) {
+                const float *pn = pc + static_cast<size_t>(qn) * (kBM * kBN);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  nxt[i] = (qn == sp || t0 + i >= nlive) ? v[h * 16 + i] : __ldcg(pn + i * kBN);
+                }
+              }
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                acc[i] = q == 0 ? cur[i] : acc[i] + cur[i];
+                cur[i] = nxt[i];
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[h * 16 + i] = acc[i];
           }
         }
-      };
-
-      if (g.mode == kModePlain) {
-        uint4 *dst = reinterpret_cast<uint4 *>(g.out + static_cast<int64_t>(t) * g.ldo +
-                                               static_cast<int64_t>(nt) * kBN);
-#pragma unroll 1
-        for (int c = 0; c < kBN / 32; ++c) {
-          float v[32];
-          chunk(c, v);
-          if (live) {
+        // transpose into staging[token][feature] (bf16)
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              dst[c * 4 + q] = make_uint4(pack_bf16(v[8 * q], v[8 * q + 1]),
-                                          pack_bf16(v[8 * q + 2], v[8 * q + 3]),
-                                          pack_bf16(v[8 * q + 4], v[8 * q + 5]),
-                                          pack_bf16(v[8 * q + 6], v[8 * q + 7]));
-            }
+        for (int i = 0; i < 32; ++i) {
+          const int t = c * 32 + i;
+          if (t < nlive) {
+            *reinterpret_cast<__nv_bfloat16 *>(staging + stg_off(t, f >> 3) + (f & 7) * 2) =
+                __float2bfloat16_rn(v[i]);
           }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&sb.acc_empty[buf]);
+      named_bar_sync(1, kEpiThreads);
+
+      const int64_t t_base = static_cast<int64_t>(mt) * kBM;
+      if (g.mode == kModePlain) {
+        // 16 chunks of 16 bytes per token row, 8 rows per pass
+        const int c = et & 15;
+        for (int t = et >> 4; t < nlive; t += kEpiThreads / 16) {
+          const uint4 w = *reinterpret_cast<const uint4 *>(staging + stg_off(t, c));
+          *reinterpret_cast<uint4 *>(g.out + (t_base + t) * g.ldo +
+                                     static_cast<int64_t>(nt) * kBN + c * 8) = w;
         }
       } else if (g.mode == kModeSwiglu) {
-        uint4 *dst = reinterpret_cast<uint4 *>(g.out + static_cast<int64_t>(t) * g.ldo +
-                                               static_cast<int64_t>(nt) * 64);
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          float gv[32], uv[32];
-          chunk(c, gv);        // gate columns [32c, 32c+32)
-          chunk(c + 2, uv);    // up columns of the same outputs
-          if (live) {
+        // 8 outputs (a gate chunk and its up chunk) per thread, 16 rows per pass
+        const int c = et & 7;
+        for (int t = et >> 3; t < nlive; t += kEpiThreads / 8) {
+          const uint4 gw = *reinterpret_cast<const uint4 *>(staging + stg_off(t, c));
+          const uint4 uw = *reinterpret_cast<const uint4 *>(staging + stg_off(t, 8 + c));
+          const uint32_t ga[4] = {gw.x, gw.y, gw.z, gw.w}, ua[4] = {uw.x, uw.y, uw.z, uw.w};
+          uint32_t o[4];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint32_t w[4];
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const int e = 8 * q + 2 * i;
-                w[i] = pack_bf16(swiglu(gv[e], uv[e]), swiglu(gv[e + 1], uv[e + 1]));
-              }
-              dst[c * 4 + q] = make_uint4(w[0], w[1], w[2], w[3]);
-            }
+          for (int i = 0; i < 4; ++i) {
+            o[i] = pack_bf16(swiglu(bf16_lo(ga[i]), bf16_lo(ua[i])),
+                             swiglu(bf16_hi(ga[i]), bf16_hi(ua[i])));
           }
+          *reinterpret_cast<uint4 *>(g.out + (t_base + t) * g.ldo + static_cast<int64_t>(nt) * 64 +
+                                     c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
         }
       } else {
-        // KV: bf16 row into the staging tile (16-byte chunk c of row r at
-        // chunk c ^ (r & 15): conflict-free for both access patterns), then
-        // K3's 8-lane row code on 16 rows at a time
-#pragma unroll 1
-        for (int c = 0; c < kBN / 32; ++c) {
-          float v[32];
-          chunk(c, v);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint4 w = make_uint4(pack_bf16(v[8 * q], v[8 * q + 1]),
-                                       pack_bf16(v[8 * q + 2], v[8 * q + 3]),
-                                       pack_bf16(v[8 * q + 4], v[8 * q + 5]),
-                                       pack_bf16(v[8 * q + 6], v[8 * q + 7]));
-            const int ch = c * 4 + q;
-            *reinterpret_cast<uint4 *>(staging + r * 256 + ((ch ^ (r & 15)) << 4)) = w;
-          }
-        }
-        named_bar_sync(1, kEpiThreads);
+        // KV: K3's 8-lane row code on 16 token rows at a time
         const int h = nt;   // head row of q|k|v
         const bool rotate = h < kv.Hq + kv.Hkv;
         const bool do_norm = (kv.flags & VJ_KV_NORM) != 0;
         const bool do_rope = (kv.flags & VJ_KV_ROPE) != 0;
         const int qscale =
             h < kv.Hq ? (kv.flags & (VJ_KV_QSCALE_DIV_SQRT_D | VJ_KV_QSCALE_MUL_RSQRT_D)) : 0;
-        for (int row = grp; row < kBM; row += kEpiThreads / 8) {
-          const int tr = mt * kBM + row;
-          if (tr >= g.rows) break;
-          const uint8_t *src = staging + row * 256;
-          const uint4 a = *reinterpret_cast<const uint4 *>(src + ((l8 ^ (row & 15)) << 4));
-          const uint4 b = *reinterpret_cast<const uint4 *>(src + (((8 + l8) ^ (row & 15)) << 4));
+        for (int row = grp; row < nlive; row += kEpiThreads / 8) {
+          const int64_t tr = t_base + row;
+          const uint4 a = *reinterpret_cast<const uint4 *>(staging + stg_off(row, l8));
+          const uint4 b = *reinterpret_cast<const uint4 *>(staging + stg_off(row, 8 + l8));
           RowSlice x = {{a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w}};
           if (rotate) {
             RowSlice cs{};
@@ -387,10 +428,8 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
           }
           store_row(kv, tr, h, h < kv.Hq ? 0 : __ldg(kv.slots + tr), x, l8);
         }
-        named_bar_sync(1, kEpiThreads);   // staging free for the next unit
       }
-      tc_fence_before();
-      mbar_arrive(&sb.acc_empty[buf]);
+      named_bar_sync(1, kEpiThreads);   // staging free for the next unit
     }
   }
 
@@ -398,6 +437,24 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, 256);
+}
+
+// Packed weight tiles: for weight tile nt (the rows weight_rows() names) and
+// K block kb, 16 KB at ((nt * kblocks) + kb) * 16 KB holding row r's 16-byte
+// chunk c at r * 128 + (c ^ (r & 7)) * 16 -- the 128-byte-swizzled K-major
+// shared-memory image the MMA reads, so one bulk copy fills a stage.
+__global__ void pack_tiles_kernel(const uint4 *__restrict__ w, uint4 *__restrict__ out, int k,
+                                  int kblocks, int swiglu, int inter, int64_t nchunks) {
+  for (int64_t o = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; o < nchunks;
+       o += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t tile = o >> 10;                 // 1024 chunks per tile
+    const int r = static_cast<int>((o >> 3) & 127), p = static_cast<int>(o & 7);
+    const int nt = static_cast<int>(tile / kblocks), kb = static_cast<int>(tile % kblocks);
+    const int c = p ^ (r & 7);
+    const int64_t row = swiglu ? (r < 64 ? 64 * nt + r : inter + 64 * nt + (r - 64))
+                               : static_cast<int64_t>(kBN) * nt + r;
+    out[o] = w[(row * k + kb * kBK + c * 8) >> 3];
+  }
 }
 
 }  // namespace
@@ -409,7 +466,8 @@ struct GemmPlan {
 };
 
 // Splits that minimise (waves of units) x (K blocks per unit + a fixed
-// per-unit cost of ~2 blocks for the pipeline fill and the epilogue).
+// per-unit cost of ~2 blocks for the pipeline fill and the epilogue) + the
+// last split's sum of the others' partials (~1 block per 32 tokens each).
 GemmPlan make_plan(int64_t rows, int n_tiles, int kblocks, int splits_req) {
   GemmPlan p{};
   p.m_tiles = static_cast<int>((rows + kBM - 1) / kBM);
@@ -417,16 +475,18 @@ GemmPlan make_plan(int64_t rows, int n_tiles, int kblocks, int splits_req) {
   p.kblocks = kblocks;
   const int sms = num_sms();
   const int64_t tiles = static_cast<int64_t>(p.m_tiles) * n_tiles;
-  const int smax = std::min(kMaxSplits, kblocks);
+  // more tiles than ticket words: no K split (such shapes fill the SMs anyway)
+  const int smax = tiles > kMaxTicketTiles ? 1 : std::min(kMaxSplits, kblocks);
   int best = 1;
   if (splits_req > 0) {
     best = std::min(splits_req, smax);
   } else {
+    const int64_t tokens = std::min<int64_t>(rows, kBM);
     int64_t best_cost = INT64_MAX;
     for (int s = 1; s <= smax; ++s) {
       const int64_t units = tiles * s;
       const int64_t waves = (units + sms - 1) / sms;
-      const int64_t cost = waves * ((kblocks + s - 1) / s + 2);
+      const int64_t cost = 32 * waves * ((kblocks + s - 1) / s + 2) + (s - 1) * tokens;
       if (cost < best_cost) {
         best_cost = cost;
         best = s;
@@ -439,11 +499,8 @@ GemmPlan make_plan(int64_t rows, int n_tiles, int kblocks, int splits_req) {
   return p;
 }
 
-size_t tickets_bytes(const GemmPlan &p) {
-  return (static_cast<size_t>(p.m_tiles) * p.n_tiles * sizeof(unsigned) + 255) & ~size_t(255);
-}
 size_t plan_workspace(const GemmPlan &p) {
-  size_t b = tickets_bytes(p);
+  size_t b = kTicketBytes;
   if (p.splits > 1) {
     b += static_cast<size_t>(p.m_tiles) * p.n_tiles * p.splits * kBM * kBN * sizeof(float);
   }
@@ -465,15 +522,18 @@ int set_smem_attr() {
 
 // Shared checks and launch. n_rows_w: weight rows; n_tiles per the mode.
 int launch_gemm(const char *who, const void *x, int64_t ldx, const void *w, int64_t n_rows_w,
-                int32_t k, int64_t rows, int n_tiles, GemmArgs &g, const KvArgs &kv,
-                int32_t splits, void *workspace, size_t workspace_bytes, int32_t *error_flag,
-                cudaStream_t stream) {
+                int32_t k, int64_t rows, int n_tiles, int32_t weight_layout, GemmArgs &g,
+                const KvArgs &kv, int32_t splits, void *workspace, size_t workspace_bytes,
+                int32_t *error_flag, cudaStream_t stream) {
   const std::string name(who);
   if (k <= 0 || k % kBK != 0) {
     return set_error(VJ_ERR_UNSUPPORTED, name + ": k must be a positive multiple of 64");
   }
   if (rows > 65536) return set_error(VJ_ERR_UNSUPPORTED, name + ": more than 65536 rows");
   if (splits < 0) return set_error(VJ_ERR_INVALID_ARGUMENT, name + ": splits < 0");
+  if (weight_layout != VJ_WEIGHTS_ROW_MAJOR && weight_layout != VJ_WEIGHTS_TILED) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT, name + ": unknown weight_layout");
+  }
   if (!x || !w) return set_error(VJ_ERR_INVALID_ARGUMENT, name + ": null pointer");
   if (ldx == 0) ldx = k;
   if (ldx < k || ldx % 8 != 0 || reinterpret_cast<uintptr_t>(x) % 16 != 0 ||
@@ -483,6 +543,12 @@ int launch_gemm(const char *who, const void *x, int64_t ldx, const void *w, int6
                             "a multiple of 8");
   }
   const GemmPlan p = make_plan(rows, n_tiles, k / kBK, splits);
+  // MMA N = the m tile's tokens rounded up to 16 (one x box of that many rows)
+  g.n_pad = p.m_tiles == 1 ? static_cast<int>((rows + 15) / 16 * 16) : kBM;
+  g.nbuf = g.n_pad <= 32 ? 8 : g.n_pad <= 64 ? 4 : 2;
+  const uint32_t x_box_rows = static_cast<uint32_t>(g.n_pad);
+  g.stage_bytes = static_cast<int>(kTileBytes + x_box_rows * kBK * 2);
+  g.stages = std::min(kMaxStages, kRingBytes / g.stage_bytes);
   const size_t need = plan_workspace(p);
   if (workspace == nullptr || workspace_bytes < need ||
       reinterpret_cast<uintptr_t>(workspace) % 256 != 0) {
@@ -492,12 +558,18 @@ int launch_gemm(const char *who, const void *x, int64_t ldx, const void *w, int6
   CUtensorMap tmx, tmw;
   int rc = encode_tmap_3d(&tmx, x, static_cast<uint64_t>(k), static_cast<uint64_t>(rows), 1,
                           static_cast<uint64_t>(ldx) * 2, static_cast<uint64_t>(ldx) * 2 * rows,
-                          kBK, kBM, 1, true);
+                          kBK, x_box_rows, 1, true);
   if (rc) return rc;
-  rc = encode_tmap_3d(&tmw, w, static_cast<uint64_t>(k), static_cast<uint64_t>(n_rows_w), 1,
-                      static_cast<uint64_t>(k) * 2, static_cast<uint64_t>(k) * 2 * n_rows_w, kBK,
-                      64, 1, true);
-  if (rc) return rc;
+  if (weight_layout == VJ_WEIGHTS_TILED) {
+    memset(&tmw, 0, sizeof(tmw));   // not read: stages come from the packed tiles
+    g.wtiles = static_cast<const uint8_t *>(w);
+  } else {
+    rc = encode_tmap_3d(&tmw, w, static_cast<uint64_t>(k), static_cast<uint64_t>(n_rows_w), 1,
+                        static_cast<uint64_t>(k) * 2, static_cast<uint64_t>(k) * 2 * n_rows_w,
+                        kBK, 64, 1, true);
+    if (rc) return rc;
+    g.wtiles = nullptr;
+  }
   if ((rc = set_smem_attr()) != VJ_OK) return rc;
   g.rows = static_cast<int>(rows);
   g.kblocks = p.kblocks;
@@ -506,7 +578,7 @@ int launch_gemm(const char *who, const void *x, int64_t ldx, const void *w, int6
   g.splits = p.splits;
   g.units = p.units;
   g.tickets = static_cast<unsigned *>(workspace);
-  g.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + tickets_bytes(p));
+  g.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + kTicketBytes);
   g.error = error_flag;
   decode_gemm_kernel<<<p.grid, kGemmThreads, kSmemBytes, stream>>>(tmx, tmw, g, kv);
   return check_launch(who);
@@ -530,11 +602,34 @@ extern "C" size_t vj_decode_gemm_workspace_size(int64_t rows, int32_t n, int32_t
   return plan_workspace(make_plan(rows, n_tiles, k / kBK, splits));
 }
 
-extern "C" vj_status vj_decode_gemm(const void *x, int64_t x_row_stride, const void *w, void *out,
-                                    int64_t out_row_stride, int64_t rows, int32_t n, int32_t k,
-                                    int32_t mode, int32_t splits, void *workspace,
-                                    size_t workspace_bytes, int32_t *error_flag,
-                                    cudaStream_t stream) {
+extern "C" vj_status vj_pack_weight_tiles(const void *w, void *out, int32_t n, int32_t k,
+                                          int32_t mode, cudaStream_t stream) {
+  using namespace vj;
+  if (n <= 0 || k <= 0 || k % kBK != 0 || n % 128 != 0) {
+    return set_error(VJ_ERR_UNSUPPORTED,
+                     "vj_pack_weight_tiles: n must be a multiple of 128 and k of 64");
+  }
+  if (mode != VJ_GEMM_PLAIN && mode != VJ_GEMM_SWIGLU) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_pack_weight_tiles: unknown mode");
+  }
+  if (!w || !out || w == out || reinterpret_cast<uintptr_t>(w) % 16 != 0 ||
+      reinterpret_cast<uintptr_t>(out) % 16 != 0) {
+    return set_error(VJ_ERR_INVALID_ARGUMENT,
+                     "vj_pack_weight_tiles: distinct 16-byte aligned w and out required");
+  }
+  const int64_t nchunks = static_cast<int64_t>(n) * k / 8;
+  const int grid = static_cast<int>(std::min<int64_t>((nchunks + 255) / 256, 148 * 16));
+  pack_tiles_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint4 *>(w),
+                                              static_cast<uint4 *>(out), k, k / kBK,
+                                              mode == VJ_GEMM_SWIGLU ? 1 : 0, n / 2, nchunks);
+  return check_launch("vj_pack_weight_tiles");
+}
+
+extern "C" vj_status vj_decode_gemm(const void *x, int64_t x_row_stride, const void *w,
+                                    int32_t weight_layout, void *out, int64_t out_row_stride,
+                                    int64_t rows, int32_t n, int32_t k, int32_t mode,
+                                    int32_t splits, void *workspace, size_t workspace_bytes,
+                                    int32_t *error_flag, cudaStream_t stream) {
   using namespace vj;
   if (rows < 0 || n <= 0) return set_error(VJ_ERR_INVALID_ARGUMENT, "vj_decode_gemm: bad shape");
   if (mode != VJ_GEMM_PLAIN && mode != VJ_GEMM_SWIGLU) {
@@ -559,12 +654,13 @@ extern "C" vj_status vj_decode_gemm(const void *x, int64_t x_row_stride, const v
   g.ldo = out_row_stride;
   KvArgs kv{};
   return launch_gemm("vj_decode_gemm", x, x_row_stride, w, n, k, rows,
-                     mode == VJ_GEMM_SWIGLU ? n / 128 : n / kBN, g, kv, splits, workspace,
-                     workspace_bytes, error_flag, stream);
+                     mode == VJ_GEMM_SWIGLU ? n / 128 : n / kBN, weight_layout, g, kv, splits,
+                     workspace, workspace_bytes, error_flag, stream);
 }
 
 extern "C" vj_status vj_qkv_gemm_kv_store(
-    const void *x, int64_t x_row_stride, const void *w_qkv, const void *q_norm_w,
+    const void *x, int64_t x_row_stride, const void *w_qkv, int32_t weight_layout,
+    const void *q_norm_w,
     const void *k_norm_w, const int32_t *positions, const int32_t *slot_mapping, void *q_out,
     void *k_cache, void *v_cache, int64_t num_tokens, int32_t hidden, int32_t num_q_heads,
     int32_t num_kv_heads, int32_t head_dim, int64_t num_blocks, int32_t block_size,
@@ -634,6 +730,6 @@ extern "C" vj_status vj_qkv_gemm_kv_store(
   a.flags = flags;
   build_rope_table(rope_theta, a.rope.inv_freq);
   return launch_gemm(who, x, x_row_stride, w_qkv, static_cast<int64_t>(heads) * kHeadDim, hidden,
-                     num_tokens, heads, g, a, splits, workspace, workspace_bytes, error_flag,
-                     stream);
+                     num_tokens, heads, weight_layout, g, a, splits, workspace, workspace_bytes,
+                     error_flag, stream);
 }

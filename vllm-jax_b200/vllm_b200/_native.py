@@ -75,12 +75,14 @@ PROTOTYPES: dict[str, tuple] = {
     "vj_add_rmsnorm": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_f32, c_vp]),
     "vj_silu_mul": (c_int, [c_vp, c_vp, c_i64, c_i32, c_vp]),
     "vj_decode_gemm_workspace_size": (c_sz, [c_i64, c_i32, c_i32, c_i32, c_i32]),
+    "vj_pack_weight_tiles": (c_int, [c_vp, c_vp, c_i32, c_i32, c_i32, c_vp]),
     "vj_decode_gemm": (c_int, [
-        c_vp, c_i64, c_vp, c_vp, c_i64,             # x, ldx, w, out, ldo
+        c_vp, c_i64, c_vp, c_i32, c_vp, c_i64,      # x, ldx, w, layout, out, ldo
         c_i64, c_i32, c_i32, c_i32, c_i32,          # rows, n, k, mode, splits
         c_vp, c_sz, c_vp, c_vp]),                   # ws, ws_bytes, err, stream
     "vj_qkv_gemm_kv_store": (c_int, [
-        c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp,  # x, ldx, w_qkv, qw, kw, positions, slots
+        c_vp, c_i64, c_vp, c_i32,                   # x, ldx, w_qkv, layout
+        c_vp, c_vp, c_vp, c_vp,                     # qw, kw, positions, slots
         c_vp, c_vp, c_vp,                           # q_out, k_cache, v_cache
         c_i64, c_i32, c_i32, c_i32, c_i32,          # T, hidden, Hq, Hkv, D
         c_i64, c_i32, c_i64, c_i64, c_i64,          # nb, bs, strides (block, token, head)
@@ -109,6 +111,7 @@ VJ_KV_QSCALE_DIV_SQRT_D, VJ_KV_QSCALE_MUL_RSQRT_D = 8, 16
 VJ_META_PREFILL, VJ_META_DECODE, VJ_META_RANGES = 0, 1, 2
 VJ_META_LAST_BLOCK_SLOT = 1
 VJ_GEMM_PLAIN, VJ_GEMM_SWIGLU = 0, 1
+VJ_WEIGHTS_ROW_MAJOR, VJ_WEIGHTS_TILED = 0, 1
 
 
 class VJError(RuntimeError):

@@ -28,7 +28,7 @@ import torch.nn.functional as F
 
 from ..kernels.decode_paged_attention import paged_decode
 from ..kernels.fused import add_rmsnorm, silu_mul
-from ..kernels.gemm import decode_gemm, gemm_workspace_bytes, qkv_gemm_kv_store
+from ..kernels.gemm import TiledWeight, decode_gemm, gemm_workspace_bytes, qkv_gemm_kv_store
 from ..kernels.kv_store import kv_store_qknorm_rope
 from ..kernels.prefill_paged_attention import paged_attention_mixed, paged_prefill
 
@@ -176,6 +176,17 @@ class Qwen3Weights:
         self.lm_head = (self.embed if cfg.tie_word_embeddings
                         else _draw((cfg.vocab_size, H), seed, 2, gen).to(device))
 
+    def pack_tiles(self) -> None:
+        """Second copy of every projection weight packed for the decode GEMMs
+        (vj_pack_weight_tiles: contiguous 16 KB swizzled tiles), kept beside
+        the row-major weights that cuBLAS uses for prefill-sized batches.
+        Costs one more copy of the projection weights in HBM."""
+        if getattr(self, "tiles", None) is not None:
+            return
+        self.tiles = [dict(qkv=TiledWeight(lw.w_qkv), o=TiledWeight(lw.w_o),
+                           gu=TiledWeight(lw.w_gate_up, "swiglu"), down=TiledWeight(lw.w_down))
+                      for lw in self.layers]
+
     def full_numpy(self):
         """Every tensor as float32 numpy (unsharded models only; for the oracle)."""
         assert self.tp_size == 1
@@ -232,11 +243,12 @@ class Qwen3Model:
         zero-filled workspace sized for every row count up to max_rows
         (allocated here, before any CUDA graph capture, and never replaced)."""
         c, w = self.cfg, self.w
+        w.pack_tiles()
         H, D = c.hidden_size, self.d
         I_l = w.layers[0].w_gate_up.shape[0] // 2
         shapes = ((w.layers[0].w_qkv.shape[0], H, "plain"), (H, self.hq * D, "plain"),
                   (2 * I_l, H, "swiglu"), (H, I_l, "plain"))
-        need = 256
+        need = 0
         for r in range(1, max_rows + 1):     # every row count: the split plan depends on it
             need = max([need] + [gemm_workspace_bytes(r, n, k, m) for n, k, m in shapes])
         self.gemm_workspace = torch.zeros(need, dtype=torch.uint8, device=w.layers[0].w_qkv.device)
@@ -251,7 +263,7 @@ class Qwen3Model:
         return x
 
     def _reduce_add_norm(self, a: torch.Tensor, w: torch.Tensor, x: torch.Tensor,
-                         w_norm: torch.Tensor, site: int):
+                         w_norm: torch.Tensor, site: int, w_tiled: TiledWeight | None = None):
         """Row-parallel GEMM a @ w.T summed over ranks, added to the residual x,
         then RMSNorm: returns (new residual, normed). Under tensor parallelism
         the GEMM writes into the NVLink buffer and one kernel reduces, adds and
@@ -262,11 +274,11 @@ class Qwen3Model:
         fused = self._fused(T)
         if c is not None and T <= c.max_rows:
             if fused:
-                decode_gemm(a, w, out=c.buffer(site, T), ws=self.gemm_workspace)
+                decode_gemm(a, w_tiled or w, out=c.buffer(site, T), ws=self.gemm_workspace)
             else:
                 torch.mm(a, w.t(), out=c.buffer(site, T))
             return c.allreduce_add_rmsnorm(site, T, x, w_norm, eps)
-        d = decode_gemm(a, w, ws=self.gemm_workspace) if fused else F.linear(a, w)
+        d = decode_gemm(a, w_tiled or w, ws=self.gemm_workspace) if fused else F.linear(a, w)
         d = self._all_reduce(d)
         return add_rmsnorm(d, w_norm, eps, residual=x)
 
@@ -278,9 +290,10 @@ class Qwen3Model:
         c = self.cfg
         T = x.shape[0]
         fused = self._fused(T)
+        tw = self.w.tiles[l] if fused else None
         if fused:
             # qkv projection + q/k norm + RoPE + KV store in one launch
-            q = qkv_gemm_kv_store(h, lw.w_qkv, kv_cache, meta.slot_mapping, meta.positions,
+            q = qkv_gemm_kv_store(h, tw["qkv"], kv_cache, meta.slot_mapping, meta.positions,
                                   lw.q_norm, lw.k_norm, self.hq, eps=c.rms_norm_eps,
                                   rope_theta=c.rope_theta, q_scale=q_scale,
                                   table=self.rope_table, ws=self.gemm_workspace)
@@ -295,13 +308,13 @@ class Qwen3Model:
                                      q_scale=q_scale, table=self.rope_table)
         o = attn_fn(q, kv_cache).reshape(T, self.hq * self.d)
         # attn_output += x; post_attention_layernorm   (qwen3.py:375-389)
-        x, h = self._reduce_add_norm(o, lw.w_o, x, lw.ln2, 0)
+        x, h = self._reduce_add_norm(o, lw.w_o, x, lw.ln2, 0, tw and tw["o"])
         if fused:
-            m = decode_gemm(h, lw.w_gate_up, "swiglu", ws=self.gemm_workspace)
+            m = decode_gemm(h, tw["gu"], "swiglu", ws=self.gemm_workspace)
         else:
             m = silu_mul(F.linear(h, lw.w_gate_up))
         # outputs = residual + mlp; next input_layernorm (or the final norm)
-        return self._reduce_add_norm(m, lw.w_down, x, w_next, 1)
+        return self._reduce_add_norm(m, lw.w_down, x, w_next, 1, tw and tw["down"])
 
     def _stack(self, x: torch.Tensor, kv_caches, meta, attn_fn,
                q_scale: str | None = None) -> torch.Tensor:

@@ -75,6 +75,9 @@ class Engine:
             self.eos_token_id = tokenizer.eos_token_id
         self.weights = weights or Qwen3Weights(self.mcfg, device, seed, self.tp_rank,
                                                self.tp_size)
+        if config.fused_gemm_max_rows > 0:
+            # packed copies of the projection weights, before the pool is sized
+            self.weights.pack_tiles()
         num_blocks = config.num_blocks
         if num_blocks <= 0:
             free, _ = torch.cuda.mem_get_info(device)
