@@ -1265,6 +1265,8 @@ def run_gemm(args, rank, world, local_rank):
                 "down": (lambda s: F.linear(xi, s["down"]),
                          lambda s: decode_gemm(xi, s["down_t"], ws=ws), H * I * 2),
             }
+            if args.gemm_op != "all":
+                ops = {k: v for k, v in ops.items() if k.startswith(args.gemm_op)}
             for name, (cub, ours, wb) in ops.items():
                 tc, to = timed(cub), timed(ours)
                 results[(R, name)] = (tc, to, wb)
@@ -1327,6 +1329,8 @@ def main():
     ap.add_argument("--fused-gemm", type=int, default=0,
                     help="e2e/c5/c4step: forwards of at most this many rows run their "
                          "projections on the fused tcgen05 GEMMs (0: cuBLAS)")
+    ap.add_argument("--gemm-op", default="all", choices=["all", "qkv", "o_proj", "gate_up", "down"],
+                    help="gemm: time one projection only (profiling)")
     ap.add_argument("--new-tokens", type=int, default=None,
                     help="profiling only (prefill): every sequence this many new tokens")
     ap.add_argument("--prefix-tokens", type=int, default=None,

@@ -54,15 +54,23 @@ def test_plain_vs_fp32(rows, n, k):
     assert torch.equal(out, again)                  # fixed split order: reproducible
 
 
-@pytest.mark.parametrize("splits", [1, 2, 5, 32])
-def test_plain_explicit_splits(splits):
+@pytest.mark.parametrize("rows,splits", [(96, 1), (96, 2), (96, 5), (96, 32),
+                                         (40, 2), (40, 3), (40, 8), (40, 32), (5, 4)])
+def test_plain_explicit_splits(rows, splits):
+    """<= 64 rows and <= 8 splits: the splits of a tile are one cluster and
+    reduce through distributed shared memory; otherwise through the
+    workspace. Same sums in the same order either way."""
     from vllm_b200.kernels.gemm import decode_gemm
-    x = _rand((96, 4096), 3)
+    x = _rand((rows, 4096), 3)
     w = _rand((1024, 4096), 4, 0.02)
     ref = x.float() @ w.float().T
     out = decode_gemm(x, w, splits=splits)
     torch.cuda.synchronize()
     _ulp_close(out, ref)
+    if rows <= 64 and splits <= 8:
+        glob = decode_gemm(x, w, splits=splits + 24)   # > 8: the workspace path
+        torch.cuda.synchronize()
+        _ulp_close(glob, ref)
 
 
 def test_plain_strided_x_and_out():

@@ -59,10 +59,12 @@ constexpr int kBN = 128;           // weight rows per tile (MMA M)
 constexpr int kBK = 64;            // K elements per stage (one 128-byte swizzle row)
 constexpr int kMaxStages = 12;
 constexpr int kTileBytes = kBN * kBK * 2;      // 16 KB: the weight tile of a K block
-constexpr int kRingBytes = 192 * 1024;         // stages: [weight tile][x box]
+constexpr int kRingBytes = 160 * 1024;         // stages: [weight tile][x box]
 constexpr int kGemmThreads = 192;
 constexpr int kEpiThreads = 128;
 constexpr int kStagingBytes = kBM * 256;       // one bf16 [token][feature] tile
+constexpr int kRedBytes = 64 * kBN * 4;        // fp32 [token][feature] partial, <= 64 tokens
+constexpr int kMaxCluster = 8;
 constexpr int kMaxSplits = 32;
 // The workspace starts with a fixed ticket area (one word per output tile of
 // a split-K call), the same for every shape, so that calls of different shapes
@@ -77,6 +79,8 @@ struct GemmArgs {
   int kblocks;              // K / 64
   int m_tiles, n_tiles, splits, units;
   int n_pad;                // tokens per m tile rounded up to 16 (MMA N), <= 128
+  int cluster;              // > 1: the splits of a tile are one thread-block cluster
+                            // and reduce through distributed shared memory
   int nbuf;                 // TMEM accumulators (256 / nbuf columns each)
   int mode;
   int stages;               // ring depth
@@ -93,11 +97,13 @@ struct GemmArgs {
 struct Smem {
   uint64_t full[kMaxStages], empty[kMaxStages];
   uint64_t acc_full[8], acc_empty[8], drain;
+  uint64_t red_ready, red_free;   // cluster reduction: partials published / consumed
   uint32_t tmem_base;
   int ticket;
 };
 constexpr int kOffStaging = kRingBytes;
-constexpr int kOffBars = kOffStaging + kStagingBytes;
+constexpr int kOffRed = kOffStaging + kStagingBytes;
+constexpr int kOffBars = kOffRed + kRedBytes;
 constexpr int kSmemBytes = kOffBars + static_cast<int>(sizeof(Smem)) + 1024;  // + alignment slack
 
 // Barrier among `count` threads that also ANDs their predicates, so that a
@@ -119,6 +125,48 @@ VJ_DEV void flag_error(int *error) {
   if (error) atomicExch(error, 1);
 }
 
+// Distributed shared memory (thread-block cluster) helpers.
+VJ_DEV uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// Arrive (release, cluster scope) on an mbarrier of a CTA in this cluster.
+VJ_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+VJ_DEV bool mbar_try_wait_acq_cluster(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded (2 s) wait with cluster-scope acquire: peers' writes published
+// before their arrivals are visible afterwards.
+VJ_DEV bool mbar_wait_cluster(uint64_t *bar, uint32_t parity) {
+  if (mbar_try_wait_acq_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait_acq_cluster(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+VJ_DEV float ld_dsmem_f32(uint32_t cluster_addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
+// All threads of all CTAs of the cluster (a lone CTA is a cluster of one).
+VJ_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+}
+
 // Unit u -> (m tile, n tile, split); m fastest so that neighbouring CTAs
 // stream the same weight tile.
 VJ_DEV void unit_coords(const GemmArgs &g, int u, int &mt, int &nt, int &sp) {
@@ -126,6 +174,24 @@ VJ_DEV void unit_coords(const GemmArgs &g, int u, int &mt, int &nt, int &sp) {
   const int r = u / g.m_tiles;
   sp = r % g.splits;
   nt = r / g.splits;
+}
+// The j-th unit of this CTA. Without a cluster: units blockIdx.x + j *
+// gridDim.x; with clusters of C CTAs: tile (cluster + j * clusters), split =
+// the CTA's rank in its cluster. False when the CTA has no j-th unit.
+VJ_DEV bool unit_at(const GemmArgs &g, int j, int &mt, int &nt, int &sp) {
+  if (g.cluster <= 1) {
+    const int u = blockIdx.x + j * gridDim.x;
+    if (u >= g.units) return false;
+    unit_coords(g, u, mt, nt, sp);
+    return true;
+  }
+  const int C = g.cluster;
+  const int tile = static_cast<int>(blockIdx.x) / C + j * (static_cast<int>(gridDim.x) / C);
+  if (tile >= g.m_tiles * g.n_tiles) return false;
+  mt = tile % g.m_tiles;
+  nt = tile / g.m_tiles;
+  sp = static_cast<int>(blockIdx.x) % C;
+  return true;
 }
 VJ_DEV int split_begin(const GemmArgs &g, int sp) {
   return static_cast<int>((static_cast<int64_t>(sp) * g.kblocks) / g.splits);
@@ -179,11 +245,16 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
       mbar_init(&sb.acc_empty[i], kEpiThreads);
     }
     mbar_init(&sb.drain, 1);
+    mbar_init(&sb.red_ready, g.cluster);
+    mbar_init(&sb.red_free, g.cluster);
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(&sb.tmem_base, 256);
   tc_fence_before();
   __syncthreads();
+  // every CTA of the cluster has initialised its barriers before any remote
+  // arrival
+  if (g.cluster > 1) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = sb.tmem_base;
   const uint32_t S = static_cast<uint32_t>(g.stages);
@@ -195,9 +266,8 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
       if (g.wtiles == nullptr) tma_prefetch_desc(&tmw);
       uint32_t it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < g.units && ok; u += gridDim.x) {
-        int mt, nt, sp;
-        unit_coords(g, u, mt, nt, sp);
+      int mt, nt, sp;
+      for (int j = 0; ok && unit_at(g, j, mt, nt, sp); ++j) {
         int wr0, wr1;
         weight_rows(g, nt, wr0, wr1);
         const int kb1 = split_begin(g, sp + 1);
@@ -236,10 +306,8 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
       const uint32_t s0 = smem_u32(smem);
       uint32_t it = 0;
       bool ok = true;
-      int j = 0;
-      for (int u = blockIdx.x; u < g.units && ok; u += gridDim.x, ++j) {
-        int mt, nt, sp;
-        unit_coords(g, u, mt, nt, sp);
+      int mt, nt, sp;
+      for (int j = 0; ok && unit_at(g, j, mt, nt, sp); ++j) {
         const int buf = j % g.nbuf;
         if (j >= g.nbuf && !mbar_wait(&sb.acc_empty[buf], ((j / g.nbuf) - 1) & 1)) {
           ok = false;
@@ -284,10 +352,13 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
     RowSlice qw, kw;
     if (g.mode == kModeKv) load_weights(kv, l8, qw, kw);
     const int nchunks = (g.n_pad + 31) / 32;
-    int j = 0;
-    for (int u = blockIdx.x; u < g.units; u += gridDim.x, ++j) {
-      int mt, nt, sp;
-      unit_coords(g, u, mt, nt, sp);
+    float *red = reinterpret_cast<float *>(smem + kOffRed);
+    uint32_t red_peer[kMaxCluster];
+    for (int q = 0; q < kMaxCluster; ++q) {
+      red_peer[q] = q < g.cluster ? mapa_shared(smem_u32(red), q) : 0u;
+    }
+    int mt, nt, sp;
+    for (int j = 0; unit_at(g, j, mt, nt, sp); ++j) {
       const int buf = j % g.nbuf;
       if (!bar_and(1, kEpiThreads, mbar_wait(&sb.acc_full[buf], (j / g.nbuf) & 1))) {
         if (et == 0) flag_error(g.error);
@@ -298,6 +369,59 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
       const int nlive = min(kBM, g.rows - mt * kBM);     // tokens of this m tile
       const int tile = nt * g.m_tiles + mt;
       const float *part = g.partials + static_cast<size_t>(tile) * g.splits * (kBM * kBN) + f;
+      int tb = 0, te = nlive;   // the tokens of the tile this CTA finishes
+      if (g.cluster > 1) {
+        // K splits of this tile = the CTAs of this cluster. Each publishes its
+        // fp32 partial [token][feature] in its own shared memory, then
+        // finishes a 1/C share of the tokens, summing the C partials in rank
+        // order through distributed shared memory.
+        const int C = g.cluster;
+        const int per = (nlive + C - 1) / C;
+        tb = min(nlive, sp * per);
+        te = min(nlive, tb + per);
+        // the peers have read this buffer's previous tile
+        if (j > 0 && !bar_and(1, kEpiThreads, mbar_wait_cluster(&sb.red_free, (j - 1) & 1))) {
+          if (et == 0) flag_error(g.error);
+          break;
+        }
+#pragma unroll 1
+        for (int c = 0; c < nchunks; ++c) {
+          float v[32];
+          tmem_ld32(tacc + c * 32, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (c * 32 + i < nlive) red[(c * 32 + i) * kBN + f] = v[i];
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&sb.acc_empty[buf]);
+        named_bar_sync(1, kEpiThreads);
+        if (et == 0) {
+          for (int q = 0; q < C; ++q) mbar_arrive_cluster(mapa_shared(smem_u32(&sb.red_ready), q));
+        }
+        if (!bar_and(1, kEpiThreads, mbar_wait_cluster(&sb.red_ready, j & 1))) {
+          if (et == 0) flag_error(g.error);
+          break;
+        }
+        for (int t = tb; t < te; ++t) {
+          float pv[kMaxCluster];
+#pragma unroll
+          for (int q = 0; q < kMaxCluster; ++q) {
+            if (q < C) pv[q] = ld_dsmem_f32(red_peer[q] + static_cast<uint32_t>(t * kBN + f) * 4u);
+          }
+          float acc = pv[0];
+#pragma unroll
+          for (int q = 1; q < kMaxCluster; ++q) {
+            if (q < C) acc += pv[q];
+          }
+          *reinterpret_cast<__nv_bfloat16 *>(staging + stg_off(t, f >> 3) + (f & 7) * 2) =
+              __float2bfloat16_rn(acc);
+        }
+        named_bar_sync(1, kEpiThreads);   // this CTA's reads of every peer are done
+        if (et == 0) {
+          for (int q = 0; q < C; ++q) mbar_arrive_cluster(mapa_shared(smem_u32(&sb.red_free), q));
+        }
+      } else {
       if (g.splits > 1) {
         // this split's partial tile to the workspace ([token][feature]:
         // coalesced); tcgen05.ld is warp-collective, so every lane loads
@@ -376,12 +500,13 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
       tc_fence_before();
       mbar_arrive(&sb.acc_empty[buf]);
       named_bar_sync(1, kEpiThreads);
+      }
 
       const int64_t t_base = static_cast<int64_t>(mt) * kBM;
       if (g.mode == kModePlain) {
         // 16 chunks of 16 bytes per token row, 8 rows per pass
         const int c = et & 15;
-        for (int t = et >> 4; t < nlive; t += kEpiThreads / 16) {
+        for (int t = tb + (et >> 4); t < te; t += kEpiThreads / 16) {
           const uint4 w = *reinterpret_cast<const uint4 *>(staging + stg_off(t, c));
           *reinterpret_cast<uint4 *>(g.out + (t_base + t) * g.ldo +
                                      static_cast<int64_t>(nt) * kBN + c * 8) = w;
@@ -389,7 +514,7 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
       } else if (g.mode == kModeSwiglu) {
         // 8 outputs (a gate chunk and its up chunk) per thread, 16 rows per pass
         const int c = et & 7;
-        for (int t = et >> 3; t < nlive; t += kEpiThreads / 8) {
+        for (int t = tb + (et >> 3); t < te; t += kEpiThreads / 8) {
           const uint4 gw = *reinterpret_cast<const uint4 *>(staging + stg_off(t, c));
           const uint4 uw = *reinterpret_cast<const uint4 *>(staging + stg_off(t, 8 + c));
           const uint32_t ga[4] = {gw.x, gw.y, gw.z, gw.w}, ua[4] = {uw.x, uw.y, uw.z, uw.w};
@@ -410,7 +535,7 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
         const bool do_rope = (kv.flags & VJ_KV_ROPE) != 0;
         const int qscale =
             h < kv.Hq ? (kv.flags & (VJ_KV_QSCALE_DIV_SQRT_D | VJ_KV_QSCALE_MUL_RSQRT_D)) : 0;
-        for (int row = grp; row < nlive; row += kEpiThreads / 8) {
+        for (int row = tb + grp; row < te; row += kEpiThreads / 8) {
           const int64_t tr = t_base + row;
           const uint4 a = *reinterpret_cast<const uint4 *>(staging + stg_off(row, l8));
           const uint4 b = *reinterpret_cast<const uint4 *>(staging + stg_off(row, 8 + l8));
@@ -435,6 +560,8 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
 
   tc_fence_before();
   __syncthreads();
+  // peers may still read this CTA's partial buffer until they pass here
+  if (g.cluster > 1) cluster_sync_all();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, 256);
 }
@@ -463,25 +590,84 @@ namespace {
 
 struct GemmPlan {
   int m_tiles, n_tiles, kblocks, splits, units, grid;
+  int cluster;   // > 1: splits reduce through distributed shared memory
 };
 
-// Splits that minimise (waves of units) x (K blocks per unit + a fixed
-// per-unit cost of ~2 blocks for the pipeline fill and the epilogue) + the
-// last split's sum of the others' partials (~1 block per 32 tokens each).
+int set_smem_attr();
+
+// Clusters of C CTAs of this kernel that fit on the GPU at once (cached per
+// device; without a device, SMs / C).
+int max_active_clusters(int C) {
+  static int cache[64][kMaxCluster + 1] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return num_sms() / C;
+  if (cache[dev][C] == 0) {
+    int n = 0;
+    if (set_smem_attr() != VJ_OK) return num_sms() / C;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(C * (num_sms() / C)), 1, 1);
+    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = static_cast<unsigned>(C);
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, decode_gemm_kernel, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = num_sms() / C;
+    }
+    cache[dev][C] = n;
+  }
+  return cache[dev][C];
+}
+
+// Work split. Cost model, in units of 1/32 K block: (rounds of units per
+// CTA) x (K blocks per unit + ~2 for the pipeline fill and the epilogue),
+// plus the partial sums of a split K.
+// * up to 64 tokens: the K splits of a tile form one cluster (C <= 8) and
+//   reduce through distributed shared memory (no workspace round trips);
+// * otherwise: splits write fp32 partials to the workspace and the last to
+//   arrive sums them (~1 block per 32 tokens and split).
 GemmPlan make_plan(int64_t rows, int n_tiles, int kblocks, int splits_req) {
   GemmPlan p{};
   p.m_tiles = static_cast<int>((rows + kBM - 1) / kBM);
   p.n_tiles = n_tiles;
   p.kblocks = kblocks;
+  p.cluster = 1;
   const int sms = num_sms();
   const int64_t tiles = static_cast<int64_t>(p.m_tiles) * n_tiles;
+  const int64_t tokens = std::min<int64_t>(rows, kBM);
+  const bool clusterable = rows <= 64 && (splits_req == 0 || splits_req <= kMaxCluster);
+  if (clusterable) {
+    const int cmax = std::min(kMaxCluster, kblocks);
+    int best = 1;
+    int64_t best_cost = INT64_MAX;
+    for (int C = 1; C <= cmax; ++C) {
+      if (splits_req > 0 && C != std::min(splits_req, cmax)) continue;
+      const int64_t ncl = C == 1 ? sms : std::max(1, max_active_clusters(C));
+      const int64_t rounds = (tiles + ncl - 1) / ncl;
+      const int64_t cost = 32 * rounds * ((kblocks + C - 1) / C + 2) + (C - 1) * tokens / 4;
+      if (cost < best_cost) {
+        best_cost = cost;
+        best = C;
+      }
+    }
+    const int64_t ncl = best == 1 ? sms : std::max(1, max_active_clusters(best));
+    p.splits = best;
+    p.cluster = best;
+    p.units = static_cast<int>(tiles * best);
+    p.grid = static_cast<int>(std::min<int64_t>(tiles, ncl) * best);
+    return p;
+  }
   // more tiles than ticket words: no K split (such shapes fill the SMs anyway)
   const int smax = tiles > kMaxTicketTiles ? 1 : std::min(kMaxSplits, kblocks);
   int best = 1;
   if (splits_req > 0) {
     best = std::min(splits_req, smax);
   } else {
-    const int64_t tokens = std::min<int64_t>(rows, kBM);
     int64_t best_cost = INT64_MAX;
     for (int s = 1; s <= smax; ++s) {
       const int64_t units = tiles * s;
@@ -501,7 +687,7 @@ GemmPlan make_plan(int64_t rows, int n_tiles, int kblocks, int splits_req) {
 
 size_t plan_workspace(const GemmPlan &p) {
   size_t b = kTicketBytes;
-  if (p.splits > 1) {
+  if (p.splits > 1 && p.cluster == 1) {
     b += static_cast<size_t>(p.m_tiles) * p.n_tiles * p.splits * kBM * kBN * sizeof(float);
   }
   return b;
@@ -576,11 +762,31 @@ int launch_gemm(const char *who, const void *x, int64_t ldx, const void *w, int6
   g.m_tiles = p.m_tiles;
   g.n_tiles = p.n_tiles;
   g.splits = p.splits;
+  g.cluster = p.cluster;
   g.units = p.units;
   g.tickets = static_cast<unsigned *>(workspace);
   g.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + kTicketBytes);
   g.error = error_flag;
-  decode_gemm_kernel<<<p.grid, kGemmThreads, kSmemBytes, stream>>>(tmx, tmw, g, kv);
+  if (p.cluster > 1) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(p.grid), 1, 1);
+    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = static_cast<unsigned>(p.cluster);
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, decode_gemm_kernel, tmx, tmw, g, kv) != cudaSuccess) {
+      return set_error(VJ_ERR_CUDA, name + ": cluster launch failed: " +
+                                        cudaGetErrorString(cudaGetLastError()));
+    }
+  } else {
+    decode_gemm_kernel<<<p.grid, kGemmThreads, kSmemBytes, stream>>>(tmx, tmw, g, kv);
+  }
   return check_launch(who);
 }
 
