@@ -29,7 +29,8 @@
 // CTA = 6 warps:
 //   warp 0      TMA producer: per K block two 64x64 weight boxes and one x box
 //               (n_pad tokens x 64), 128-byte swizzle, into a ring of up to 12
-//               stages in 192 KB
+//               stages in 192 KB (160 KB with a cluster reduction); packed
+//               weights come as one 16 KB bulk copy per stage instead
 //   warp 1      TMEM owner + MMA issuer: tcgen05.mma kind::f16, M = 128,
 //               N = n_pad, K = 16, both operands K-major in shared memory; the
 //               256 TMEM columns hold 2 (n_pad > 64), 4 (> 32) or 8
@@ -39,7 +40,12 @@
 //               split the fp32 partials go through the workspace (the last of
 //               a tile's splits to arrive -- atomicInc ticket, threadfence-
 //               reduction pattern, no CTA ever waits for another -- sums them
-//               in split order, so results do not depend on timing); the bf16
+//               in split order, so results do not depend on timing); on
+//               request (2-8 splits, <= 64 tokens) the splits of a tile are
+//               one thread-block cluster instead and sum their partials in
+//               rank order through distributed shared memory (remote mbarrier
+//               arrivals, bounded waits), each rank finishing 1/C of the
+//               tokens; the bf16
 //               tile is transposed into a [token][feature] shared-memory tile,
 //               from which the mode's row pass stores (PLAIN), applies SiLU-mul
 //               (SWIGLU) or runs K3's 8-lane row code (KV)
@@ -59,7 +65,11 @@ constexpr int kBN = 128;           // weight rows per tile (MMA M)
 constexpr int kBK = 64;            // K elements per stage (one 128-byte swizzle row)
 constexpr int kMaxStages = 12;
 constexpr int kTileBytes = kBN * kBK * 2;      // 16 KB: the weight tile of a K block
-constexpr int kRingBytes = 160 * 1024;         // stages: [weight tile][x box]
+// Shared memory: the stage ring ([weight tile][x box] per stage), then the
+// bf16 staging tile; with a cluster reduction the ring gives up 32 KB to the
+// fp32 partial buffer: [ring 160 KB][staging][red] instead of [ring 192 KB][staging].
+constexpr int kRingBytes = 192 * 1024;
+constexpr int kRingBytesCluster = 160 * 1024;
 constexpr int kGemmThreads = 192;
 constexpr int kEpiThreads = 128;
 constexpr int kStagingBytes = kBM * 256;       // one bf16 [token][feature] tile
@@ -101,9 +111,9 @@ struct Smem {
   uint32_t tmem_base;
   int ticket;
 };
-constexpr int kOffStaging = kRingBytes;
-constexpr int kOffRed = kOffStaging + kStagingBytes;
-constexpr int kOffBars = kOffRed + kRedBytes;
+constexpr int kOffRed = kRingBytesCluster + kStagingBytes;
+constexpr int kOffBars = kRingBytes + kStagingBytes;
+static_assert(kOffRed + kRedBytes == kOffBars, "shared-memory layout");
 constexpr int kSmemBytes = kOffBars + static_cast<int>(sizeof(Smem)) + 1024;  // + alignment slack
 
 // Barrier among `count` threads that also ANDs their predicates, so that a
@@ -345,7 +355,7 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constan
     const int quarter = warp & 3;                    // TMEM lane quarter of this warp
     const int f = quarter * 32 + lane;               // feature (weight row) of the tile
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    uint8_t *staging = smem + kOffStaging;
+    uint8_t *staging = smem + (g.cluster > 1 ? kRingBytesCluster : kRingBytes);
     // K3 state (KV mode): 16 groups of 8 lanes
     const int grp = et >> 3, l8 = et & 7;
     const unsigned grp_mask = 0xffu << (8 * (grp & 3));
@@ -624,13 +634,12 @@ int max_active_clusters(int C) {
   return cache[dev][C];
 }
 
-// Work split. Cost model, in units of 1/32 K block: (rounds of units per
-// CTA) x (K blocks per unit + ~2 for the pipeline fill and the epilogue),
-// plus the partial sums of a split K.
-// * up to 64 tokens: the K splits of a tile form one cluster (C <= 8) and
-//   reduce through distributed shared memory (no workspace round trips);
-// * otherwise: splits write fp32 partials to the workspace and the last to
-//   arrive sums them (~1 block per 32 tokens and split).
+// Work split. Automatic: the split count minimising, in units of 1/32 K
+// block, (waves of units) x (K blocks per unit + ~2 for the pipeline fill and
+// the epilogue) + the partial sums (~1 block per 32 tokens and split); splits
+// write fp32 partials to the workspace and the last to arrive sums them. On
+// request (2-8 splits at <= 64 tokens) the splits of a tile form one cluster
+// and reduce through distributed shared memory instead.
 GemmPlan make_plan(int64_t rows, int n_tiles, int kblocks, int splits_req) {
   GemmPlan p{};
   p.m_tiles = static_cast<int>((rows + kBM - 1) / kBM);
@@ -640,26 +649,17 @@ GemmPlan make_plan(int64_t rows, int n_tiles, int kblocks, int splits_req) {
   const int sms = num_sms();
   const int64_t tiles = static_cast<int64_t>(p.m_tiles) * n_tiles;
   const int64_t tokens = std::min<int64_t>(rows, kBM);
-  const bool clusterable = rows <= 64 && (splits_req == 0 || splits_req <= kMaxCluster);
+  // the cluster reduction is taken on request (an explicit split of 2-8 at
+  // <= 64 tokens): measured, it does not beat the workspace reduction with the
+  // deeper ring that the automatic choice keeps
+  const bool clusterable = rows <= 64 && splits_req >= 2 && splits_req <= kMaxCluster;
   if (clusterable) {
-    const int cmax = std::min(kMaxCluster, kblocks);
-    int best = 1;
-    int64_t best_cost = INT64_MAX;
-    for (int C = 1; C <= cmax; ++C) {
-      if (splits_req > 0 && C != std::min(splits_req, cmax)) continue;
-      const int64_t ncl = C == 1 ? sms : std::max(1, max_active_clusters(C));
-      const int64_t rounds = (tiles + ncl - 1) / ncl;
-      const int64_t cost = 32 * rounds * ((kblocks + C - 1) / C + 2) + (C - 1) * tokens / 4;
-      if (cost < best_cost) {
-        best_cost = cost;
-        best = C;
-      }
-    }
-    const int64_t ncl = best == 1 ? sms : std::max(1, max_active_clusters(best));
-    p.splits = best;
-    p.cluster = best;
-    p.units = static_cast<int>(tiles * best);
-    p.grid = static_cast<int>(std::min<int64_t>(tiles, ncl) * best);
+    const int C = std::min(splits_req, kblocks);
+    const int64_t ncl = C == 1 ? sms : std::max(1, max_active_clusters(C));
+    p.splits = C;
+    p.cluster = C;
+    p.units = static_cast<int>(tiles * C);
+    p.grid = static_cast<int>(std::min<int64_t>(tiles, ncl) * C);
     return p;
   }
   // more tiles than ticket words: no K split (such shapes fill the SMs anyway)
@@ -734,7 +734,8 @@ int launch_gemm(const char *who, const void *x, int64_t ldx, const void *w, int6
   g.nbuf = g.n_pad <= 32 ? 8 : g.n_pad <= 64 ? 4 : 2;
   const uint32_t x_box_rows = static_cast<uint32_t>(g.n_pad);
   g.stage_bytes = static_cast<int>(kTileBytes + x_box_rows * kBK * 2);
-  g.stages = std::min(kMaxStages, kRingBytes / g.stage_bytes);
+  g.stages = std::min(kMaxStages,
+                      (p.cluster > 1 ? kRingBytesCluster : kRingBytes) / g.stage_bytes);
   const size_t need = plan_workspace(p);
   if (workspace == nullptr || workspace_bytes < need ||
       reinterpret_cast<uintptr_t>(workspace) % 256 != 0) {
