@@ -1172,6 +1172,114 @@ def run_c4step(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def run_mixedstep(args, rank, world, local_rank):
+    """One chunked-prefill step of Qwen3-8B (the engine's forward_mixed):
+    --batch decode rows (default 128) at context --context, packed first,
+    then 2 prompt chunks of 2048 new tokens after cached prefixes of 1024 and
+    3072 tokens. Each layer's attention over both kinds is one
+    vj_paged_attention_mixed launch. CUDA events around --steps eager
+    forwards; per-kernel device time and launches of one step (torch
+    profiler) on stderr. The line's value: ms per step."""
+    import collections
+
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    from vllm_b200 import _native
+    from vllm_b200.kernels.kv_store import rope_table
+    from vllm_b200.kernels.metadata import RangesMeta
+    from vllm_b200.model.qwen3 import Qwen3Model, Qwen3Weights, get_config
+    if world > 1:
+        raise SystemExit("--workload mixedstep runs on one GPU")
+    nd, L = args.batch or 128, args.context
+    chunks = [(1024, 2048), (3072, 2048)]            # (cached prefix, new tokens)
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    cfg = get_config("Qwen3-8B")
+    m = Qwen3Model(Qwen3Weights(cfg, dev, seed=0))
+    bs, D, Hkv, Hq = 16, cfg.head_dim, cfg.num_key_value_heads, cfg.num_attention_heads
+    ctx = [L] * nd + [p + n for p, n in chunks]
+    S = len(ctx)
+    pages = [(c + bs - 1) // bs for c in ctx]
+    width = max(pages)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7)
+    perm = torch.randperm(sum(pages), generator=gen, device=dev).to(torch.int32)
+    bt = torch.full((S, width), -1, dtype=torch.int32, device=dev)
+    o = 0
+    for s, p in enumerate(pages):
+        bt[s, :p] = perm[o:o + p]
+        o += p
+    nb = sum(pages) + 8
+    kv = [torch.randn((2, nb, bs, Hkv, D), generator=gen, device=dev).to(torch.bfloat16)
+          for _ in range(cfg.num_hidden_layers)]
+    pos, cu = [], [0]
+    for s in range(S):
+        start, n = (ctx[s] - 1, 1) if s < nd else chunks[s - nd]
+        pos += list(range(start, start + n))
+        cu.append(cu[-1] + n)
+    T = cu[-1]
+    pos_t = torch.tensor(pos, dtype=torch.int32, device=dev)
+    seq_of = torch.repeat_interleave(torch.arange(S, device=dev),
+                                     torch.tensor([cu[i + 1] - cu[i] for i in range(S)],
+                                                  device=dev))
+    slots = (bt[seq_of, (pos_t // bs).long()] * bs + pos_t % bs).to(torch.int32)
+    rows = torch.tensor(cu[1:], dtype=torch.int64, device=dev) - 1
+    meta = RangesMeta(torch.randint(0, cfg.vocab_size, (T,), generator=gen, device=dev)
+                      .to(torch.int32), pos_t, slots, bt,
+                      torch.tensor(cu, dtype=torch.int32, device=dev),
+                      torch.tensor(ctx, dtype=torch.int32, device=dev), S, T,
+                      max(n for _, n in chunks), rows, rows, rows)
+    m.decode_workspace = torch.empty(
+        max(_native.load().vj_paged_attention_mixed_workspace_size(nd, Hq, D, 0), 16),
+        dtype=torch.uint8, device=dev)
+    m.rope_table = rope_table(dev, cfg.rope_theta, max(ctx) + 1)
+
+    def step():
+        return m.forward_mixed(meta, kv, nd, rows)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    before = _native.launch_count
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    launches = _native.launch_count - before
+    ms = e0.elapsed_time(e1) / args.steps
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step()
+        torch.cuda.synchronize()
+    agg = collections.defaultdict(lambda: [0, 0.0])
+    for e in prof.key_averages():
+        if e.device_time_total > 0:
+            agg[e.key][0] += e.count
+            agg[e.key][1] += e.device_time_total
+    tot = sum(v[1] for v in agg.values()) or 1.0
+    print(f"per-kernel device time of one mixed step ({nd} decode rows at context {L}, "
+          f"chunks {chunks}; torch profiler):", file=sys.stderr)
+    for k, (c, t) in sorted(agg.items(), key=lambda kv: -kv[1][1])[:16]:
+        print(f"  {t / 1000:8.3f} ms {100 * t / tot:5.1f}%  launches {c:5d}  {k[:100]}",
+              file=sys.stderr)
+    line = {
+        "metric": f"Qwen3-8B chunked-prefill step ms ({nd} decode rows + 2 x 2048-token chunks)",
+        "value": round(ms, 4), "unit": "ms", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init N(0,0.02) weights, N(0,1) KV, random tables)",
+        "config": {"workload": "mixed chunked step (forward_mixed, eager)", "decode_rows": nd,
+                   "context": L, "chunks": chunks, "tokens": T,
+                   "library_launches_per_step": launches // args.steps},
+        "gpu_launches": launches,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_gemm(args, rank, world, local_rank):
     """The four projections of one Qwen3-8B decoder layer at decode batch
     sizes, cuBLAS (+ the separate K3 / SiLU-mul launches) against this
@@ -1306,12 +1414,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["e2e", "decode", "prefill", "kvstore", "c5", "c4step",
-                                           "gemm"],
+                                           "gemm", "mixedstep"],
                     default="e2e",
                     help="e2e (default): C4 Qwen3-8B output tok/s, tensor parallel over "
                          "--gpus; decode: C3 paged decode GB/s; prefill: C2 TFLOP/s; "
                          "kvstore: K3 GB/s; c5: Qwen3-32B chunked prefill tok/s; c4step: "
-                         "one decode step; gemm: decode-step projections vs cuBLAS")
+                         "one decode step; gemm: decode-step projections vs cuBLAS; "
+                         "mixedstep: one chunked-prefill step")
     ap.add_argument("--model", default=None, help="e2e: model preset (default Qwen3-8B)")
     ap.add_argument("--max-num-seqs", type=int, default=None, help="e2e: scheduler seats")
     ap.add_argument("--tp", type=int, default=None,
@@ -1371,6 +1480,8 @@ def main():
             run_c4step(args, rank, world, local_rank)
         elif args.workload == "gemm":
             run_gemm(args, rank, world, local_rank)
+        elif args.workload == "mixedstep":
+            run_mixedstep(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:
