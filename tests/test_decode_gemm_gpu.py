@@ -186,3 +186,36 @@ def test_packed_weight_tiles_bit_identical(rows):
     q2 = qkv_gemm_kv_store(x, TiledWeight(wq), c2, slots, pos, qn, kn, 8, table=table)
     torch.cuda.synchronize()
     assert torch.equal(q1, q2) and torch.equal(c1, c2)
+
+
+@pytest.mark.parametrize("rows,splits", [(16, 2), (61, 4), (1, 8)])
+def test_cluster_reduction_many_tiles_all_modes(rows, splits):
+    """Cluster split-K with more weight tiles than clusters (each cluster
+    walks several tiles: its partial buffer is reused once every peer has
+    read it), in all three epilogues; against the workspace reduction of the
+    same split count (> 8 forces it) or the plain path."""
+    from vllm_b200.kernels.fused import silu_mul
+    from vllm_b200.kernels.gemm import decode_gemm, qkv_gemm_kv_store
+    from vllm_b200.kernels.kv_store import kv_store_qknorm_rope, rope_table
+    x = _rand((rows, 4096), 21)
+    w = _rand((24576, 4096), 22, 0.02)                  # 192 weight tiles
+    ref = x.float() @ w.float().T
+    out = decode_gemm(x, w, splits=splits)
+    torch.cuda.synchronize()
+    _ulp_close(out, ref)
+    sw = decode_gemm(x, w, "swiglu", splits=splits)
+    torch.cuda.synchronize()
+    _ulp_close(sw.float(), silu_mul(out).float())      # same arithmetic on ~equal inputs
+    x, wq, qn, kn, cache, slots, pos = _qkv_case(rows, 32, 8, 4096, seed=rows + 100)
+    table = rope_table(x.device, 1e6, 4096)
+    c1, c2 = cache.clone(), cache.clone()
+    q1 = qkv_gemm_kv_store(x, wq, c1, slots, pos, qn, kn, 32, table=table, splits=splits)
+    qkv = decode_gemm(x, wq, splits=splits)
+    D = 128
+    q, k, v = torch.split(qkv, [32 * D, 8 * D, 8 * D], -1)
+    q2 = kv_store_qknorm_rope(q.reshape(rows, 32, D).contiguous(),
+                              k.reshape(rows, 8, D).contiguous(),
+                              v.reshape(rows, 8, D).contiguous(), c2, slots, pos, qn, kn,
+                              table=table)
+    torch.cuda.synchronize()
+    assert torch.equal(q1, q2) and torch.equal(c1, c2)  # same splits, same sums
